@@ -1,0 +1,222 @@
+// ref_harness.cpp -- TEST INFRASTRUCTURE ONLY (the checker, never the product).
+//
+// extern "C" shims over the reference's UNMODIFIED token-selection sources
+// (src/sampling/{sampling,grammar_vocab,token-trie}.cpp of rye-001/Qwenium),
+// compiled from where they lie by oracle/Makefile into oracle/_ref/*.so.
+// Tests, __graft_entry__.smoke() and bench.py's cpu_baseline / reference leg
+// load these libraries through ctypes (oracle/oracle.py); nothing in the
+// product links or calls them.
+//
+// What the shims add on top of the reference API:
+//   * seeding of TemperatureSampler::gen_ (private; src/sampling/sampling.h:92,
+//     seeded from std::random_device in sampling.cpp:114-122). Access uses the
+//     explicit-instantiation access rule, which is standard C++ and leaves the
+//     class layout untouched;
+//   * the per-row uniform draw u the reference's own engine will consume:
+//     std::generate_canonical<double,53> on a COPY of the engine, taken right
+//     before sample(), so the GPU path can be fed the identical u;
+//   * a copy of the logits after sample(): the reference mutates them in place
+//     (pruning, grammar mask, repetition penalty, temperature), which pins the
+//     transform stage separately from the selection stage.
+#include "sampling.h"
+#include "grammar_vocab.h"
+#include "token-trie.h"
+
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <random>
+#include <thread>
+#include <string>
+#include <unordered_set>
+#include <vector>
+
+namespace {
+
+// ---- access to TemperatureSampler::gen_ ------------------------------------
+// [temp.explicit]/12: access checking does not apply to the names used in an
+// explicit instantiation, so &TemperatureSampler::gen_ may be named here.
+template <typename Tag>
+struct MemberPtr {
+    static typename Tag::type value;
+};
+template <typename Tag>
+typename Tag::type MemberPtr<Tag>::value;
+
+template <typename Tag, typename Tag::type P>
+struct StoreMemberPtr {
+    struct Filler {
+        Filler() { MemberPtr<Tag>::value = P; }
+    };
+    static Filler filler;
+};
+template <typename Tag, typename Tag::type P>
+typename StoreMemberPtr<Tag, P>::Filler StoreMemberPtr<Tag, P>::filler;
+
+struct GenTag {
+    typedef std::mt19937 qwenium::TemperatureSampler::*type;
+};
+template struct StoreMemberPtr<GenTag, &qwenium::TemperatureSampler::gen_>;
+
+std::mt19937& engine_of(qwenium::TemperatureSampler& s) {
+    return s.*(MemberPtr<GenTag>::value);
+}
+
+struct Vocab {
+    std::vector<std::string> strs;
+};
+
+}  // namespace
+
+extern "C" {
+
+// TemperatureSampler::sample (sampling.cpp:137-194) on one row.
+//   seed      : the engine is std::mt19937(seed) before the call.
+//   u_out     : generate_canonical<double,53> of a copy of that engine, i.e.
+//               the uniform discrete_distribution consumes if it draws.
+//   drew_out  : 1 if the engine advanced (discrete_distribution drew), else 0
+//               (it does not draw for a single survivor, or for T<=0).
+//   logits_out: optional [V] copy of the logits after sample() returned.
+int qwref_temperature_sample(const float* logits, int V, const int32_t* hist, int H,
+                             float temperature, float rep_penalty, int rep_lookback,
+                             int top_k, float top_p, uint32_t seed, double* u_out,
+                             int* drew_out, float* logits_out) {
+    qwenium::TemperatureSampler s(temperature, rep_penalty, rep_lookback, top_k, top_p);
+    std::mt19937& gen = engine_of(s);
+    gen = std::mt19937(seed);
+    std::mt19937 probe = gen;
+    const double u = std::generate_canonical<double, 53>(probe);
+    if (u_out) *u_out = u;
+    std::vector<float> lv(logits, logits + V);
+    std::vector<int32_t> hv(hist, hist + (H > 0 ? H : 0));
+    const int id = s.sample(lv, hv, {});
+    if (drew_out) *drew_out = (gen == std::mt19937(seed)) ? 0 : 1;
+    if (logits_out) std::memcpy(logits_out, lv.data(), sizeof(float) * (size_t)V);
+    return id;
+}
+
+// GreedySampler::sample (sampling.cpp:98-108) on one row.
+int qwref_greedy_sample(const float* logits, int V, const int32_t* hist, int H,
+                        float rep_penalty, int rep_lookback, float* logits_out) {
+    qwenium::GreedySampler s(rep_penalty, rep_lookback);
+    std::vector<float> lv(logits, logits + V);
+    std::vector<int32_t> hv(hist, hist + (H > 0 ? H : 0));
+    const int id = s.sample(lv, hv, {});
+    if (logits_out) std::memcpy(logits_out, lv.data(), sizeof(float) * (size_t)V);
+    return id;
+}
+
+// ---- vocabulary / trie / grammar handles -----------------------------------
+void* qwref_vocab_new(const char* const* strs, const int32_t* lens, int V) {
+    Vocab* v = new Vocab();
+    v->strs.reserve((size_t)V);
+    for (int i = 0; i < V; ++i) v->strs.emplace_back(strs[i], (size_t)lens[i]);
+    return v;
+}
+void qwref_vocab_free(void* v) { delete static_cast<Vocab*>(v); }
+
+void* qwref_trie_new(void* vocab) {
+    qwenium::TokenTrie* t = new qwenium::TokenTrie();
+    t->build(static_cast<Vocab*>(vocab)->strs);
+    return t;
+}
+void qwref_trie_free(void* t) { delete static_cast<qwenium::TokenTrie*>(t); }
+
+void* qwref_grammar_parse(const char* gbnf) {
+    auto g = qwenium::GrammarVocab::parse_impl(std::string(gbnf));
+    return g.release();
+}
+void qwref_grammar_free(void* g) { delete static_cast<qwenium::GrammarVocab*>(g); }
+void qwref_grammar_set_trie(void* g, void* trie) {
+    static_cast<qwenium::GrammarVocab*>(g)->set_token_trie(static_cast<qwenium::TokenTrie*>(trie));
+}
+// get_valid_tokens (grammar_vocab.cpp:571-755): ascending ids; returns the
+// full count even when it exceeds cap (only the first cap are written).
+int qwref_grammar_valid(void* g, void* vocab, int32_t* out, int cap) {
+    std::vector<int32_t> ids =
+        static_cast<qwenium::GrammarVocab*>(g)->get_valid_tokens(static_cast<Vocab*>(vocab)->strs);
+    const int n = (int)ids.size();
+    for (int i = 0; i < n && i < cap; ++i) out[i] = ids[i];
+    return n;
+}
+void qwref_grammar_accept(void* g, int32_t id, void* vocab) {
+    static_cast<qwenium::GrammarVocab*>(g)->accept_token(id, static_cast<Vocab*>(vocab)->strs);
+}
+int qwref_grammar_accepting(void* g) {
+    return static_cast<qwenium::GrammarVocab*>(g)->is_accepting_state() ? 1 : 0;
+}
+void qwref_grammar_reset(void* g) { static_cast<qwenium::GrammarVocab*>(g)->reset(); }
+
+// The full Sampler::sample path with a grammar, an EOS id and/or a pruning
+// keep-set attached (sampling.cpp:12-81): exercises apply_vocab_pruning,
+// apply_grammar_constraints (EOS allowance, stuck-grammar EOS forcing) and
+// the lazily built trie. kind 0 = GreedySampler, 1 = TemperatureSampler.
+// grammar may be NULL; keep_ids with n_keep < 0 means "no pruning".
+int qwref_sampler_sample_full(int kind, float temperature, float rep_penalty, int rep_lookback,
+                              int top_k, float top_p, void* grammar, void* vocab, int32_t eos_id,
+                              const int32_t* keep_ids, int n_keep, const float* logits, int V,
+                              const int32_t* hist, int H, uint32_t seed, double* u_out,
+                              float* logits_out) {
+    std::unordered_set<int32_t> keep;
+    if (n_keep >= 0) keep.insert(keep_ids, keep_ids + n_keep);
+    std::vector<float> lv(logits, logits + V);
+    std::vector<int32_t> hv(hist, hist + (H > 0 ? H : 0));
+    const std::vector<std::string> empty;
+    const std::vector<std::string>& strs = vocab ? static_cast<Vocab*>(vocab)->strs : empty;
+    int id;
+    if (kind == 0) {
+        qwenium::GreedySampler s(rep_penalty, rep_lookback);
+        if (grammar) s.set_grammar(static_cast<qwenium::GrammarVocab*>(grammar));
+        if (n_keep >= 0) s.set_pruned_vocab(&keep);
+        if (eos_id >= 0) s.set_eos_token_id(eos_id);
+        id = s.sample(lv, hv, strs);
+        if (u_out) *u_out = 0.0;
+    } else {
+        qwenium::TemperatureSampler s(temperature, rep_penalty, rep_lookback, top_k, top_p);
+        if (grammar) s.set_grammar(static_cast<qwenium::GrammarVocab*>(grammar));
+        if (n_keep >= 0) s.set_pruned_vocab(&keep);
+        if (eos_id >= 0) s.set_eos_token_id(eos_id);
+        std::mt19937& gen = engine_of(s);
+        gen = std::mt19937(seed);
+        std::mt19937 probe = gen;
+        if (u_out) *u_out = std::generate_canonical<double, 53>(probe);
+        id = s.sample(lv, hv, strs);
+    }
+    if (logits_out) std::memcpy(logits_out, lv.data(), sizeof(float) * (size_t)V);
+    return id;
+}
+
+// Many rows through TemperatureSampler::sample, split over n_threads
+// std::threads with one sampler per row (the way BASELINE's CPU figure (ii)
+// runs the reference). Used to time the reference on the host cores.
+int qwref_temperature_sample_batch(const float* logits, int B, int V, int64_t row_stride,
+                                   const float* temperature, const int32_t* top_k,
+                                   const float* top_p, const float* rep_penalty,
+                                   const int32_t* rep_lookback, const int32_t* hist,
+                                   int hist_stride, const int32_t* hist_len,
+                                   const uint32_t* seeds, int32_t* out, int n_threads) {
+    if (n_threads < 1) n_threads = 1;
+    std::vector<std::thread> pool;
+    std::atomic<int> next{0};
+    for (int t = 0; t < n_threads; ++t) {
+        pool.emplace_back([&]() {
+            for (int b = next.fetch_add(1); b < B; b = next.fetch_add(1)) {
+                out[b] = qwref_temperature_sample(
+                    logits + (size_t)b * (size_t)row_stride, V, hist + (size_t)b * (size_t)hist_stride,
+                    hist_len[b], temperature[b], rep_penalty[b], rep_lookback[b], top_k[b], top_p[b],
+                    seeds[b], nullptr, nullptr, nullptr);
+            }
+        });
+    }
+    for (auto& th : pool) th.join();
+    return 0;
+}
+
+// std::generate_canonical<double,53>(std::mt19937(seed)) -- the u the
+// reference's engine yields first for a given seed.
+double qwref_first_uniform(uint32_t seed) {
+    std::mt19937 g(seed);
+    return std::generate_canonical<double, 53>(g);
+}
+
+}  // extern "C"
