@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 token-selection path (qsamp).
+
+Workload (N=1): the batched-server-decode parameter distribution
+(per-row T~U[0.2,1.2], top-k in {0,20,40,100}, top-p~U[0.8,1.0],
+frequency/presence penalties over a 256-id history) at B=256, V=151936, fp32
+logits -- the B=256 / V=151936 point of the headline metric. A step is one
+batched selection call over B rows. Under torchrun every rank runs its own B
+rows (weak scaling, no collective on the data path).
+
+  value  -- rows/s over all ranks, inputs resident in HBM, device-timed with
+            CUDA events (max over ranks); inputs rotate over copies whose
+            total exceeds L2, so every step reads logits from HBM.
+  e2e    -- the same through qsamp_sample_host: pinned host logits, history
+            and params copied in, ids and results copied out, every step.
+  roofline -- algorithmic bytes of the selection kernel per launch over its
+            mean launch time, against the measured HBM copy bandwidth.
+
+`--impl reference` times the reference's own CPU sampler (src/sampling
+compiled unmodified with its Release flags, oracle/_ref) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B_DEFAULT = 256
+V = 151936
+HIST = 256
+
+
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(key):
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        d = json.load(f)
+    return d.get(key)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def algorithmic_bytes_per_row(V_, hist_len, bytes_per_logit=4, mask=False):
+    # logits + history ids + params/u/result (SURVEY 8d per-row figure)
+    return V_ * bytes_per_logit + (((V_ + 31) // 32) * 4 if mask else 0) + 4 * hist_len + 64
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    from qwenium_b200 import qsamp
+    from qwenium_b200 import workloads as W
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    B = args.batch
+    cfg = W.config2(seed=1000 + rank, B=B)
+    ctx = qsamp.Context(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    # rotating copies: > 2x L2 between reuses of a buffer
+    bytes_one = B * V * 4
+    ncopies = max(2, int(np.ceil(3 * 126e6 / bytes_one)) + 1)
+    xs = [torch.from_numpy(cfg["logits"]).to(dev) for _ in range(ncopies)]
+    hist = torch.from_numpy(cfg["hist"]).to(dev)
+    ids = torch.empty(B, dtype=torch.int32, device=dev)
+    res = torch.empty((B, 32), dtype=torch.uint8, device=dev)
+
+    def step(i):
+        ctx.sample_batch(xs[i % ncopies], cfg["params"], hist=hist, hist_len=cfg["hist_len"], u=cfg["u"],
+                         out_ids=ids, out_results=res, stream=stream.cuda_stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    # per-launch kernel time: the same loop with an event pair per launch
+    per = []
+    for i in range(min(args.steps, 20)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step(i)
+        b.record(stream)
+        b.synchronize()
+        per.append(a.elapsed_time(b))
+    launch_ms = statistics.mean(per)
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+
+    # e2e through the host entry point with pinned buffers
+    e2e_rows_s = None
+    h2d = d2h = 0
+    if not args.no_e2e:
+        hx = torch.from_numpy(cfg["logits"]).pin_memory()
+        hh = torch.from_numpy(cfg["hist"]).pin_memory()
+        hl = cfg["hist_len"]
+        e2e_steps = max(3, min(args.steps, 20))
+        for _ in range(2):
+            ctx.sample_host(hx.numpy(), cfg["params"], hist=hh.numpy(), hist_len=hl, u=cfg["u"])
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            ctx.sample_host(hx.numpy(), cfg["params"], hist=hh.numpy(), hist_len=hl, u=cfg["u"])
+        el = time.perf_counter() - t0
+        el_t = torch.tensor([el], device=dev)
+        if world > 1:
+            dist.all_reduce(el_t, op=dist.ReduceOp.MAX)
+        e2e_rows_s = world * B * e2e_steps / float(el_t.item())
+        h2d = B * V * 4 + B * HIST * 4 + B * (48 + 8 + 4)
+        d2h = B * (4 + 32)
+
+    # B=10 latency point (device-timed, same parameter distribution)
+    b10 = None
+    if rank == 0 and not args.no_b10:
+        c10 = W.config2(seed=77, B=10)
+        x10 = [torch.from_numpy(c10["logits"]).to(dev) for _ in range(8)]
+        h10 = torch.from_numpy(c10["hist"]).to(dev)
+        i10 = torch.empty(10, dtype=torch.int32, device=dev)
+        for i in range(5):
+            ctx.sample_batch(x10[i % 8], c10["params"], hist=h10, hist_len=c10["hist_len"], u=c10["u"], out_ids=i10)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n10 = 50
+        a.record(stream)
+        for i in range(n10):
+            ctx.sample_batch(x10[i % 8], c10["params"], hist=h10, hist_len=c10["hist_len"], u=c10["u"], out_ids=i10,
+                             stream=stream.cuda_stream)
+        b.record(stream)
+        torch.cuda.synchronize()
+        t10 = a.elapsed_time(b) / n10
+        b10 = {"ms_per_step": round(t10, 4), "rows_per_s": round(10 / (t10 * 1e-3), 1)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(cfg, seconds=args.cpu_seconds)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peaks()
+    alg = algorithmic_bytes_per_row(V, HIST) * B
+    achieved = alg / (launch_ms * 1e-3) / 1e9
+    traffic = ncu_traffic("config2-B256")
+    ms_step = ms / args.steps
+    out = {
+        "metric": "sampled rows/s (batched token selection, B=256, V=151936)",
+        "value": round(world * B * args.steps / (ms * 1e-3), 1),
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded config-2 distribution)",
+        "config": {"workload": "config2-B256: batched server decode parameters at B=256, V=151936 fp32",
+                   "B_per_gpu": B, "V": V, "history": HIST, "parallelism": f"rows x{world}",
+                   "l2": f"rotating {ncopies} input copies ({ncopies * bytes_one / 1e6:.0f} MB) > L2"},
+        "e2e": {"value": round(e2e_rows_s, 1) if e2e_rows_s else None, "unit": "rows/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
+                     "bytes_per_launch": alg, "launch_ms": round(launch_ms, 4)},
+        "clocks": clk.summary(),
+    }
+    if b10:
+        out["b10"] = b10
+    if cpu:
+        out["cpu_baseline"] = cpu
+    print(json.dumps(out))
+
+
+# ------------------------------------------------------------------ CPU legs
+def _ref_batch(lib, cfg, rows, threads):
+    import ctypes
+
+    P = ctypes.c_void_p
+    x = np.ascontiguousarray(cfg["logits"][rows])
+    p = cfg["params"][rows]
+    T = np.ascontiguousarray(p["temperature"], np.float32)
+    k = np.ascontiguousarray(p["top_k"], np.int32)
+    tp = np.ascontiguousarray(p["top_p"], np.float32)
+    rep = np.ascontiguousarray(p["repetition_penalty"], np.float32)
+    lb = np.ascontiguousarray(p["repetition_lookback"], np.int32)
+    h = np.ascontiguousarray(cfg["hist"][rows])
+    hl = np.ascontiguousarray(cfg["hist_len"][rows])
+    seeds = np.ascontiguousarray(cfg["seeds"][rows], np.uint32)
+    out = np.empty(len(rows), np.int32)
+    f = lambda a: a.ctypes.data_as(P)
+    lib.qwref_temperature_sample_batch(f(x), len(rows), x.shape[1], x.shape[1], f(T), f(k), f(tp), f(rep), f(lb), f(h),
+                                       h.shape[1], f(hl), f(seeds), f(out), threads)
+    return out
+
+
+def cpu_baseline(cfg, seconds=10.0):
+    """The reference's own CPU sampler (Release build) on the host cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    if O.ref_available("release"):
+        lib = O.ref_lib("release")
+        kind = "reference"
+        B = len(cfg["params"])
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            rows = np.arange(B)
+            _ref_batch(lib, cfg, rows, threads)
+            done += B
+        el = time.perf_counter() - t0
+        sample = (f"{done} rows of the config2-B256 workload through TemperatureSampler::sample "
+                  "(frequency/presence have no reference code and are off), one sampler per row, "
+                  f"{threads} std::threads")
+    else:
+        kind = "port"
+        B = len(cfg["params"])
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            O.oracle_sample(cfg["logits"], cfg["params"], cfg["hist"], cfg["hist_len"], None, cfg["u"],
+                            n_threads=threads)
+            done += B
+        el = time.perf_counter() - t0
+        sample = f"{done} rows of config2-B256 through the C restatement, {threads} threads"
+    return {"value": round(done / el, 2), "unit": "rows/s", "cores": threads, "kind": kind, "sample": sample}
+
+
+def run_reference(args):
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    from qwenium_b200 import workloads as W
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    if not O.ref_available("release"):
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libqwref_release.so was not built"}))
+        return
+    cfg = W.config2(seed=1000, B=args.batch)
+    lib = O.ref_lib("release")
+    threads = os.cpu_count() or 1
+    # each step: a bounded sample of the B-row workload (whole rows, all cores)
+    rows_per_step = max(threads, min(args.batch, 4 * threads))
+    rows = np.arange(rows_per_step) % args.batch
+    for _ in range(args.warmup):
+        _ref_batch(lib, cfg, rows, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _ref_batch(lib, cfg, rows, threads)
+    el = time.perf_counter() - t0
+    v = rows_per_step * args.steps / el
+    out = {
+        "impl": "reference",
+        "metric": "sampled rows/s (batched token selection, B=256, V=151936)",
+        "value": round(v, 2),
+        "unit": "rows/s",
+        "n_gpus": env_int("WORLD_SIZE", 1),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded config-2 distribution)",
+        "config": {"workload": "config2-B256: batched server decode parameters at B=256, V=151936 fp32",
+                   "rows_per_step": rows_per_step, "V": V},
+        "cpu_baseline": {"value": round(v, 2), "unit": "rows/s", "cores": threads, "kind": "reference",
+                         "sample": f"{rows_per_step} rows per step through TemperatureSampler::sample (Release "
+                                   "flags, frequency/presence off: no reference code)"},
+        "e2e": {"value": round(v, 2), "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="qsamp", choices=["qsamp", "reference"])
+    ap.add_argument("--batch", type=int, default=B_DEFAULT)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-b10", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

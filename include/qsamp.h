@@ -1,0 +1,169 @@
+/* qsamp.h -- C ABI of the B200 token-selection library (libqsamp.so).
+ *
+ * Replaces the per-step token selection of rye-001/Qwenium
+ * (src/sampling/sampling.{h,cpp}) with a batched sm_100a kernel pipeline.
+ * Plain C types only; every entry point returns a qsamp_status and never
+ * throws. Reference citations are path:line in the Qwenium tree.
+ *
+ * Semantics per row (the reference's stage order, sampling.cpp:137-194):
+ *   soft-cap (Gemma-2 style cap*tanh(x/cap), a model-graph op in the
+ *   reference, layers/attention.cpp:30-36) -> allow-mask (vocab pruning
+ *   sampling.cpp:12-18, grammar sampling.cpp:25-81) -> repetition penalty
+ *   (sampling.cpp:124-135) -> frequency/presence penalty (extension) ->
+ *   T <= 0: first argmax | x /= T -> sort -> top-k -> top-p -> softmax ->
+ *   discrete draw against u (sampling.cpp:158-193).
+ * Results are bit-identical to the reference evaluated in source order
+ * (IEEE float, sequential sums); equal logits are ordered by ascending id.
+ */
+#ifndef QSAMP_H
+#define QSAMP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    QSAMP_OK = 0,
+    QSAMP_ERR_INVALID_ARG = 1, /* message names the argument, expected and actual values */
+    QSAMP_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+    QSAMP_ERR_UNSUPPORTED = 3, /* valid request this build does not serve (message says which) */
+    QSAMP_ERR_DEVICE = 4,      /* the kernel reported an internal limit (message says which) */
+    QSAMP_ERR_NO_MEMORY = 5,
+    QSAMP_ERR_IO = 6           /* keep-list file unreadable (vocab_utils.h:12-37 throws) */
+} qsamp_status;
+
+typedef enum { QSAMP_F32 = 0, QSAMP_BF16 = 1 } qsamp_dtype;
+
+/* Per-row sampling parameters: one TemperatureSampler / GreedySampler
+ * configuration (sampling.h:53-93) per slot. 48 bytes, naturally aligned. */
+typedef struct qsamp_row_params {
+    float temperature;           /* <= 0: greedy (sampling.cpp:149-152)               */
+    int32_t top_k;               /* 0 or >= V: off (sampling.cpp:165-166)             */
+    float top_p;                 /* active when 0 < p < 1 (sampling.cpp:168-179)      */
+    float repetition_penalty;    /* 1.0: off (sampling.cpp:124-135)                   */
+    int32_t repetition_lookback; /* window = last min(lookback, len) ids               */
+    float frequency_penalty;     /* extension: l -= count(id) * f over the window      */
+    float presence_penalty;      /* extension: l -= p for ids present in the window    */
+    float softcap;               /* extension: cap * tanh(l / cap) first; 0: off       */
+    int32_t force_token;         /* >= 0: stuck grammar, only this id (logit 0.0),
+                                    sampling.cpp:40-60; -1: off                        */
+    int32_t flags;               /* reserved, must be 0                                */
+    uint64_t seed;               /* Philox key when the batch has no u                 */
+} qsamp_row_params;
+
+/* Per-row outcome (device memory). */
+typedef struct qsamp_row_result {
+    int32_t token;    /* selected id (Sampler::sample's return value)                 */
+    int32_t position; /* rank of token among the sorted survivors                     */
+    int32_t n_keep;   /* survivors after top-k/top-p (1 when greedy)                  */
+    int32_t drew;     /* 1 if the discrete draw consumed u (2+ survivors)             */
+    float sum_exp;    /* top-p denominator (sampling.cpp:171); 0 when top-p is off    */
+    float sum_keep;   /* softmax denominator over survivors (sampling.cpp:184)        */
+    float max_logit;  /* largest logit after temperature                              */
+    float prob;       /* probability of token                                         */
+} qsamp_row_result;
+
+typedef struct qsamp_ctx qsamp_ctx;
+
+/* One batched selection step: the body of the server's batched decode loop
+ * (http_server.cpp:300-306 calls Sampler::sample once per slot; this call
+ * serves all slots of a BatchedDecodeFunc step, inference_server.h:177-178). */
+typedef struct qsamp_batch {
+    const void* logits;               /* DEVICE [B][row_stride] of dtype (the output
+                                         head's [V,B] tensor, forward_pass_base.cpp:138-158) */
+    qsamp_dtype dtype;
+    int32_t B, V;
+    int64_t row_stride;               /* elements between rows, >= V                  */
+    const qsamp_row_params* params;   /* HOST [B]                                     */
+    const int32_t* hist;              /* DEVICE [B][hist_stride] ids, newest last, or NULL */
+    int32_t hist_stride;
+    const int32_t* hist_len;          /* HOST [B] valid ids per row (NULL: hist_stride) */
+    const uint32_t* masks;            /* DEVICE allow-bits, bit i%32 of word i/32, or NULL */
+    int64_t mask_stride;              /* words between row masks; 0: one shared mask   */
+    const double* u;                  /* HOST [B] uniforms in [0,1), or NULL: Philox    */
+    uint64_t rng_offset;              /* Philox counter offset (when u is NULL)         */
+    int32_t* out_ids;                 /* DEVICE [B] or NULL                             */
+    qsamp_row_result* out_results;    /* DEVICE [B] or NULL                             */
+    int32_t* out_top_ids;             /* DEVICE [B][top_cap] sorted survivors, or NULL  */
+    float* out_top_probs;             /* DEVICE [B][top_cap], or NULL                   */
+    int32_t top_cap;
+} qsamp_batch;
+
+/* Context bound to one CUDA device (ownership as in sampling.h:46-50: the
+ * sampler owns its scratch; all batch pointers are borrowed for the call). */
+qsamp_status qsamp_create(int32_t device, qsamp_ctx** out);
+void qsamp_destroy(qsamp_ctx* ctx);
+/* Last error message of this context (valid until the next call). */
+const char* qsamp_last_error(const qsamp_ctx* ctx);
+
+/* Batched selection, stream-ordered on `stream` (a cudaStream_t; NULL: the
+ * legacy default stream). Replaces the per-slot loop of
+ * QwenServerIntegration::run_batched_decode (http_server.cpp:300-306). */
+qsamp_status qsamp_sample(qsamp_ctx* ctx, const qsamp_batch* batch, void* stream);
+
+/* The same with every pointer in HOST memory (logits, hist, masks, outputs):
+ * copies in, selects, copies out, synchronises. This is the drop-in for
+ * Sampler::sample(std::vector<float>& logits, ...) (sampling.h:22-24), whose
+ * logits live on the host. */
+qsamp_status qsamp_sample_host(qsamp_ctx* ctx, const qsamp_batch* batch);
+
+/* Host helpers for the allow-mask. -------------------------------------- */
+
+/* Pack ids into allow-bits (words = ceil(V/32), zeroed first); ids outside
+ * [0,V) are ignored. Replaces the vector<bool> of sampling.cpp:62-64 and the
+ * keep-set lookup of apply_vocab_pruning (sampling.cpp:12-18). */
+qsamp_status qsamp_pack_ids(const int32_t* ids, int64_t n, int32_t V, uint32_t* mask_out);
+
+/* The grammar allow-mask of Sampler::apply_grammar_constraints
+ * (sampling.cpp:25-81) from GrammarVocab::get_valid_tokens ids
+ * (grammar_vocab.cpp:571-755): valid ids; if `accepting`, also
+ * eos_string_id (the first vocab entry equal to "<|endoftext|>" or
+ * "<|im_end|>", see qsamp_find_eos_string) and eos_token_id when in range.
+ * With no valid id the grammar is stuck: *force_token_out = eos_string_id
+ * (logit forced to 0.0, all others -inf) and the mask is cleared; otherwise
+ * *force_token_out = -1. */
+qsamp_status qsamp_grammar_mask(const int32_t* valid_ids, int64_t n_valid, int32_t accepting,
+                                int32_t eos_string_id, int32_t eos_token_id, int32_t V,
+                                uint32_t* mask_out, int32_t* force_token_out);
+
+/* First id whose string is "<|endoftext|>" or "<|im_end|>" (the scan of
+ * sampling.cpp:53-58 and :67-71), or -1. strs[i] has lens[i] bytes. */
+int32_t qsamp_find_eos_string(const char* const* strs, const int32_t* lens, int32_t V);
+
+/* Vocab-pruning keep list, file format [u32 count][u32 id]*count
+ * (load_keep_list, vocab_utils.h:12-37), packed into allow-bits. */
+qsamp_status qsamp_keep_list_mask(const char* path, int32_t V, uint32_t* mask_out);
+
+/* AND two allow-masks word by word (pruning AND grammar). */
+qsamp_status qsamp_mask_and(const uint32_t* a, const uint32_t* b, int64_t words, uint32_t* out);
+
+/* Vocab-sharded selection (tensor-parallel output head). ----------------
+ * Rank r holds logits[:, v_offset : v_offset + V_local] of a V_total vocab.
+ * Step 1 (each rank): the local top-k (k <= 1024) after the row transform,
+ * as (value, global id) pairs sorted by (value desc, id asc), plus the local
+ * max. Step 2: an all-gather of the [B][k] candidates over the ranks (NCCL),
+ * then qsamp_merge_topk on every rank: the global top-k of the union
+ * (ties to the lower global id), top-p, softmax and the draw, exactly as the
+ * unsharded path. Penalties use global ids (hist holds global ids). */
+qsamp_status qsamp_shard_topk(qsamp_ctx* ctx, const qsamp_batch* local_batch, int32_t v_offset,
+                              int32_t V_total, int32_t k, float* cand_vals, int32_t* cand_ids,
+                              void* stream);
+qsamp_status qsamp_merge_topk(qsamp_ctx* ctx, int32_t n_ranks, int32_t B, int32_t k,
+                              const float* all_vals, const int32_t* all_ids,
+                              const qsamp_row_params* params, const double* u, uint64_t rng_offset,
+                              int32_t* out_ids, qsamp_row_result* out_results, void* stream);
+
+/* Counters since creation (observability). */
+typedef struct qsamp_counters {
+    uint64_t calls, rows, logit_bytes, gather_rounds;
+    double last_call_us;
+} qsamp_counters;
+qsamp_status qsamp_get_counters(const qsamp_ctx* ctx, qsamp_counters* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QSAMP_H */

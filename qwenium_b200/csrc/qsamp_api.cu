@@ -1,0 +1,559 @@
+// qsamp_api.cu -- the C ABI of include/qsamp.h: context, argument checks,
+// soft-cap tables, launches, and the host-side allow-mask helpers.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "qsamp_device.h"
+
+extern "C" cudaError_t qs_launch_rows(const qs::QsLaunch* a, int clusters, int cl, size_t smem, cudaStream_t st);
+extern "C" cudaError_t qs_kernel_attrs(size_t smem);
+extern "C" cudaError_t qs_kernel_static_smem(size_t* out);
+extern "C" cudaError_t qs_max_clusters(int cl, size_t smem, int* out);
+extern "C" cudaError_t qs_launch_lut(float* lut, float cap, cudaStream_t st);
+extern "C" cudaError_t qs_launch_shard(const qs::QsLaunch* a, int clusters, int cl, size_t smem, int v_offset,
+                                       int k, float* cand_vals, int32_t* cand_ids, cudaStream_t st);
+extern "C" cudaError_t qs_launch_merge(int n_ranks, int B, int k, const float* vals, const int32_t* ids,
+                                       const qsamp_row_params* params, const double* u, unsigned long long off,
+                                       int32_t* out_ids, qsamp_row_result* out_res, cudaStream_t st);
+
+namespace {
+
+constexpr int kMaxRounds = 64;
+
+template <typename T>
+struct DevBuf {
+    T* p = nullptr;
+    size_t n = 0;
+    cudaError_t ensure(size_t want) {
+        if (want <= n) return cudaSuccess;
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+        cudaError_t e = cudaMalloc((void**)&p, want * sizeof(T));
+        if (e == cudaSuccess) n = want;
+        return e;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+};
+
+}  // namespace
+
+struct qsamp_ctx {
+    int device = 0;
+    int num_sms = 0;
+    int smem_optin = 0;
+    std::string err;
+    std::mutex mu;
+    DevBuf<qsamp_row_params> params;
+    DevBuf<int32_t> hist_len;
+    DevBuf<double> u;
+    DevBuf<qsamp_row_result> results;
+    DevBuf<int> status;
+    DevBuf<float> luts;
+    float lut_caps[qs::MAX_LUT] = {0, 0, 0, 0};
+    int lut_next = 0;
+    // staging for the host-memory entry point
+    DevBuf<unsigned char> h_logits;
+    DevBuf<int32_t> h_hist, h_ids, h_top_ids;
+    DevBuf<uint32_t> h_masks;
+    DevBuf<float> h_top_probs;
+    DevBuf<qsamp_row_result> h_results;
+    cudaStream_t stream = nullptr;
+    size_t attrs_smem = 0;
+    size_t max_dyn = 0;    // largest dynamic shared memory a CTA of the kernel may use
+    qsamp_counters ctr = {};
+};
+
+namespace {
+
+qsamp_status fail(qsamp_ctx* c, qsamp_status s, const char* fmt, ...) {
+    if (c) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        c->err = buf;
+    }
+    return s;
+}
+
+qsamp_status cuda_fail(qsamp_ctx* c, cudaError_t e, const char* what) {
+    return fail(c, QSAMP_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct Plan {
+    int cl, n_s, clusters;
+    size_t smem;
+};
+
+// Smallest cluster whose slices fit the per-CTA shared-memory limit; for
+// small batches, wider clusters while every row still gets its own cluster.
+qsamp_status plan_for(qsamp_ctx* c, int B, int V, Plan& out) {
+    if (c->max_dyn == 0) {
+        size_t st = 0;
+        cudaError_t e = qs_kernel_static_smem(&st);
+        if (e != cudaSuccess) return cuda_fail(c, e, "cudaFuncGetAttributes");
+        c->max_dyn = (size_t)c->smem_optin - st;
+        e = qs_kernel_attrs(c->max_dyn);
+        if (e != cudaSuccess) return cuda_fail(c, e, "cudaFuncSetAttribute");
+        c->attrs_smem = c->max_dyn;
+    }
+    const int sizes[5] = {1, 2, 4, 8, 16};
+    int first = -1;
+    for (int i = 0; i < 5; ++i) {
+        const int n_s = qs::align_up((V + sizes[i] - 1) / sizes[i], 8);
+        if ((size_t)qs::smem_layout(n_s).total <= c->max_dyn) {
+            first = i;
+            break;
+        }
+    }
+    if (first < 0)
+        return fail(c, QSAMP_ERR_UNSUPPORTED, "V=%d exceeds the largest vocabulary one 16-CTA cluster holds (%d)", V,
+                    16 * (int)((c->max_dyn - (size_t)qs::smem_layout(0).total) / 4 / 8 * 8));
+    int pick = first;
+    for (int i = first; i < 5; ++i) {
+        const int cl = sizes[i];
+        const int n_s = qs::align_up((V + cl - 1) / cl, 8);
+        const size_t smem = (size_t)qs::smem_layout(n_s).total;
+        int mc = 0;
+        cudaError_t e = qs_max_clusters(cl, smem, &mc);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            mc = 0;
+        }
+        if (mc <= 0) break;
+        if (i == first || mc >= B) pick = i;
+        if (mc < B) break;
+    }
+    const int cl = sizes[pick];
+    out.cl = cl;
+    out.n_s = qs::align_up((V + cl - 1) / cl, 8);
+    out.smem = (size_t)qs::smem_layout(out.n_s).total;
+    int mc = 0;
+    cudaError_t e = qs_max_clusters(cl, out.smem, &mc);
+    if (e != cudaSuccess || mc <= 0)
+        return cuda_fail(c, e == cudaSuccess ? cudaErrorInvalidConfiguration : e, "cudaOccupancyMaxActiveClusters");
+    out.clusters = mc < B ? mc : B;
+    return QSAMP_OK;
+}
+
+qsamp_status validate(qsamp_ctx* c, const qsamp_batch* b) {
+    if (!b) return fail(c, QSAMP_ERR_INVALID_ARG, "batch: expected non-NULL");
+    if (b->B < 0) return fail(c, QSAMP_ERR_INVALID_ARG, "B: expected >= 0, got %d", b->B);
+    if (b->B == 0) return QSAMP_OK;
+    if (b->V < 1) return fail(c, QSAMP_ERR_INVALID_ARG, "V: expected >= 1, got %d", b->V);
+    if (b->row_stride < b->V)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "row_stride: expected >= V (%d), got %lld", b->V, (long long)b->row_stride);
+    if (!b->logits) return fail(c, QSAMP_ERR_INVALID_ARG, "logits: expected non-NULL");
+    if (b->dtype != QSAMP_F32 && b->dtype != QSAMP_BF16)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "dtype: expected QSAMP_F32 or QSAMP_BF16, got %d", (int)b->dtype);
+    if (!b->params) return fail(c, QSAMP_ERR_INVALID_ARG, "params: expected non-NULL");
+    if (!b->out_ids && !b->out_results)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "out_ids/out_results: expected at least one non-NULL");
+    if (b->top_cap < 0 || b->top_cap > qs::KMAX)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "top_cap: expected [0,%d], got %d", qs::KMAX, b->top_cap);
+    if (b->top_cap > 0 && (!b->out_top_ids || !b->out_top_probs))
+        return fail(c, QSAMP_ERR_INVALID_ARG, "out_top_ids/out_top_probs: expected non-NULL when top_cap > 0");
+    if (b->hist && b->hist_stride < 1)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "hist_stride: expected >= 1 with hist, got %d", b->hist_stride);
+    const long long words = (b->V + 31) / 32;
+    if (b->masks && b->mask_stride != 0 && b->mask_stride < words)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "mask_stride: expected 0 or >= %lld words, got %lld", words,
+                    (long long)b->mask_stride);
+    for (int r = 0; r < b->B; ++r) {
+        const qsamp_row_params& p = b->params[r];
+        if (p.flags != 0) return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].flags: expected 0, got %d", r, p.flags);
+        if (std::isnan(p.temperature))
+            return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].temperature: expected a number, got NaN", r);
+        if (p.force_token < -1 || p.force_token >= b->V)
+            return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].force_token: expected -1 or [0,%d), got %d", r, b->V,
+                        p.force_token);
+        if (b->hist) {
+            const int len = b->hist_len ? b->hist_len[r] : b->hist_stride;
+            if (len < 0 || len > b->hist_stride)
+                return fail(c, QSAMP_ERR_INVALID_ARG, "hist_len[%d]: expected [0,%d], got %d", r, b->hist_stride, len);
+            const bool pen = p.repetition_penalty != 1.0f || p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
+            const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
+            const long long w = (long long)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
+            if (pen && w > qs::HIST_MAX)
+                return fail(c, QSAMP_ERR_UNSUPPORTED, "row %d: penalty window of %lld ids exceeds %d", r, w,
+                            qs::HIST_MAX);
+        }
+        if (b->u) {
+            const double uu = b->u[r];
+            if (!(uu >= 0.0 && uu < 1.0))
+                return fail(c, QSAMP_ERR_INVALID_ARG, "u[%d]: expected [0,1), got %g", r, uu);
+        }
+    }
+    return QSAMP_OK;
+}
+
+qsamp_status ensure_luts(qsamp_ctx* c, const qsamp_batch* b, cudaStream_t st) {
+    if (b->dtype != QSAMP_BF16) return QSAMP_OK;
+    cudaError_t e = c->luts.ensure((size_t)qs::MAX_LUT * 65536);
+    if (e != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(soft-cap tables)");
+    for (int r = 0; r < b->B; ++r) {
+        const float cap = b->params[r].softcap;
+        if (!(cap > 0.0f)) continue;
+        bool have = false;
+        for (int q = 0; q < qs::MAX_LUT; ++q) have |= c->lut_caps[q] == cap;
+        if (have) continue;
+        // a slot not used by this batch
+        int slot = -1;
+        for (int t = 0; t < qs::MAX_LUT && slot < 0; ++t) {
+            const int q = (c->lut_next + t) % qs::MAX_LUT;
+            bool used = false;
+            for (int r2 = 0; r2 < b->B && !used; ++r2) used = c->lut_caps[q] != 0.0f && b->params[r2].softcap == c->lut_caps[q];
+            if (!used) slot = q;
+        }
+        if (slot < 0) continue;  // more than MAX_LUT caps: remaining rows compute tanh per element
+        e = qs_launch_lut(c->luts.p + (size_t)slot * 65536, cap, st);
+        if (e != cudaSuccess) return cuda_fail(c, e, "soft-cap table launch");
+        c->lut_caps[slot] = cap;
+        c->lut_next = (slot + 1) % qs::MAX_LUT;
+    }
+    return QSAMP_OK;
+}
+
+qsamp_status read_status(qsamp_ctx* c) {
+    int st = 0;
+    cudaError_t e = cudaMemcpy(&st, c->status.p, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(c, e, "reading the device status");
+    switch (st) {
+        case qs::DEV_OK: return QSAMP_OK;
+        case qs::DEV_TOPK_TOO_LARGE: return fail(c, QSAMP_ERR_DEVICE, "device: top-k above the sorted-candidate limit");
+        case qs::DEV_ROUNDS_EXHAUSTED:
+            return fail(c, QSAMP_ERR_DEVICE,
+                        "device: a row needed more sorted elements than one gather round holds (token -1)");
+        default: return fail(c, QSAMP_ERR_DEVICE, "device: internal status %d", st);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+qsamp_status qsamp_create(int32_t device, qsamp_ctx** out) {
+    if (!out) return QSAMP_ERR_INVALID_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        return QSAMP_ERR_INVALID_ARG;
+    }
+    qsamp_ctx* c = new (std::nothrow) qsamp_ctx();
+    if (!c) return QSAMP_ERR_NO_MEMORY;
+    c->device = device;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+    cudaDeviceGetAttribute(&c->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    cudaError_t e = c->status.ensure(1);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        delete c;
+        return QSAMP_ERR_CUDA;
+    }
+    *out = c;
+    return QSAMP_OK;
+}
+
+void qsamp_destroy(qsamp_ctx* c) {
+    if (!c) return;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(c->device);
+    c->params.release();
+    c->hist_len.release();
+    c->u.release();
+    c->results.release();
+    c->status.release();
+    c->luts.release();
+    c->h_logits.release();
+    c->h_hist.release();
+    c->h_ids.release();
+    c->h_top_ids.release();
+    c->h_masks.release();
+    c->h_top_probs.release();
+    c->h_results.release();
+    if (c->stream) cudaStreamDestroy(c->stream);
+    cudaSetDevice(prev);
+    delete c;
+}
+
+const char* qsamp_last_error(const qsamp_ctx* c) { return c ? c->err.c_str() : "no context"; }
+
+static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream_t st) {
+    qsamp_status s = validate(c, b);
+    if (s != QSAMP_OK || b->B == 0) return s;
+    const int B = b->B;
+    cudaError_t e;
+    if ((e = c->params.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(params)");
+    if ((e = c->results.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(results)");
+    if ((e = cudaMemcpyAsync(c->params.p, b->params, sizeof(qsamp_row_params) * B, cudaMemcpyHostToDevice, st)) !=
+        cudaSuccess)
+        return cuda_fail(c, e, "copying params");
+    const int32_t* d_hl = nullptr;
+    if (b->hist && b->hist_len) {
+        if ((e = c->hist_len.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(hist_len)");
+        if ((e = cudaMemcpyAsync(c->hist_len.p, b->hist_len, sizeof(int32_t) * B, cudaMemcpyHostToDevice, st)) !=
+            cudaSuccess)
+            return cuda_fail(c, e, "copying hist_len");
+        d_hl = c->hist_len.p;
+    }
+    const double* d_u = nullptr;
+    if (b->u) {
+        if ((e = c->u.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(u)");
+        if ((e = cudaMemcpyAsync(c->u.p, b->u, sizeof(double) * B, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+            return cuda_fail(c, e, "copying u");
+        d_u = c->u.p;
+    }
+    s = ensure_luts(c, b, st);
+    if (s != QSAMP_OK) return s;
+    Plan plan;
+    s = plan_for(c, B, b->V, plan);
+    if (s != QSAMP_OK) return s;
+    if ((e = cudaMemsetAsync(c->status.p, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail(c, e, "status reset");
+
+    qs::QsLaunch a = {};
+    a.logits = b->logits;
+    a.dtype = (int)b->dtype;
+    a.B = B;
+    a.V = b->V;
+    a.row_stride = b->row_stride;
+    const size_t esz = b->dtype == QSAMP_BF16 ? 2 : 4;
+    a.vec_ok = ((uintptr_t)b->logits % 16 == 0) && ((size_t)b->row_stride * esz % 16 == 0);
+    a.params = c->params.p;
+    a.hist = b->hist;
+    a.hist_stride = b->hist_stride;
+    a.hist_len = d_hl;
+    a.masks = b->masks;
+    a.mask_stride = b->mask_stride;
+    a.u = d_u;
+    a.philox_offset = b->rng_offset;
+    a.luts = c->luts.p;
+    for (int q = 0; q < qs::MAX_LUT; ++q) a.lut_caps[q] = c->lut_caps[q];
+    a.results = b->out_results ? b->out_results : c->results.p;
+    a.out_ids = b->out_ids;
+    a.top_ids = b->top_cap > 0 ? b->out_top_ids : nullptr;
+    a.top_probs = b->top_cap > 0 ? b->out_top_probs : nullptr;
+    a.top_cap = b->top_cap;
+    a.status = c->status.p;
+    a.n_s = plan.n_s;
+    a.max_rounds = kMaxRounds;
+    e = qs_launch_rows(&a, plan.clusters, plan.cl, plan.smem, st);
+    if (e != cudaSuccess) return cuda_fail(c, e, "selection kernel launch");
+    c->ctr.calls += 1;
+    c->ctr.rows += (uint64_t)B;
+    c->ctr.logit_bytes += (uint64_t)B * (uint64_t)b->V * esz;
+    return QSAMP_OK;
+}
+
+qsamp_status qsamp_sample(qsamp_ctx* c, const qsamp_batch* b, void* stream) {
+    if (!c) return QSAMP_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> g(c->mu);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != c->device) cudaSetDevice(c->device);
+    qsamp_status s = sample_locked(c, b, (cudaStream_t)stream);
+    if (prev != c->device) cudaSetDevice(prev);
+    return s;
+}
+
+qsamp_status qsamp_sample_host(qsamp_ctx* c, const qsamp_batch* hb) {
+    if (!c) return QSAMP_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> g(c->mu);
+    qsamp_status s = validate(c, hb);
+    if (s != QSAMP_OK || hb->B == 0) return s;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != c->device) cudaSetDevice(c->device);
+    const auto t0 = std::chrono::steady_clock::now();
+    cudaStream_t st = c->stream;
+    const int B = hb->B, V = hb->V;
+    const size_t esz = hb->dtype == QSAMP_BF16 ? 2 : 4;
+    qsamp_batch db = *hb;
+    cudaError_t e;
+    do {
+        if ((e = c->h_logits.ensure((size_t)B * V * esz)) != cudaSuccess) break;
+        if ((e = cudaMemcpy2DAsync(c->h_logits.p, (size_t)V * esz, hb->logits, (size_t)hb->row_stride * esz,
+                                   (size_t)V * esz, (size_t)B, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+            break;
+        db.logits = c->h_logits.p;
+        db.row_stride = V;
+        if (hb->hist) {
+            if ((e = c->h_hist.ensure((size_t)B * hb->hist_stride)) != cudaSuccess) break;
+            if ((e = cudaMemcpyAsync(c->h_hist.p, hb->hist, sizeof(int32_t) * (size_t)B * hb->hist_stride,
+                                     cudaMemcpyHostToDevice, st)) != cudaSuccess)
+                break;
+            db.hist = c->h_hist.p;
+        }
+        if (hb->masks) {
+            const size_t words = (size_t)(V + 31) / 32;
+            const size_t rows = hb->mask_stride == 0 ? 1 : (size_t)B;
+            const size_t stride = hb->mask_stride == 0 ? words : (size_t)hb->mask_stride;
+            if ((e = c->h_masks.ensure(rows * stride)) != cudaSuccess) break;
+            if ((e = cudaMemcpyAsync(c->h_masks.p, hb->masks, sizeof(uint32_t) * rows * stride, cudaMemcpyHostToDevice,
+                                     st)) != cudaSuccess)
+                break;
+            db.masks = c->h_masks.p;
+        }
+        if ((e = c->h_ids.ensure(B)) != cudaSuccess) break;
+        if ((e = c->h_results.ensure(B)) != cudaSuccess) break;
+        db.out_ids = c->h_ids.p;
+        db.out_results = c->h_results.p;
+        if (hb->top_cap > 0) {
+            if ((e = c->h_top_ids.ensure((size_t)B * hb->top_cap)) != cudaSuccess) break;
+            if ((e = c->h_top_probs.ensure((size_t)B * hb->top_cap)) != cudaSuccess) break;
+            db.out_top_ids = c->h_top_ids.p;
+            db.out_top_probs = c->h_top_probs.p;
+        }
+    } while (0);
+    if (e != cudaSuccess) {
+        if (prev != c->device) cudaSetDevice(prev);
+        return cuda_fail(c, e, "staging host inputs");
+    }
+    s = sample_locked(c, &db, st);
+    if (s == QSAMP_OK) {
+        do {
+            if (hb->out_ids && (e = cudaMemcpyAsync(hb->out_ids, c->h_ids.p, sizeof(int32_t) * B,
+                                                    cudaMemcpyDeviceToHost, st)) != cudaSuccess)
+                break;
+            if (hb->out_results && (e = cudaMemcpyAsync(hb->out_results, c->h_results.p,
+                                                        sizeof(qsamp_row_result) * B, cudaMemcpyDeviceToHost, st)) !=
+                                       cudaSuccess)
+                break;
+            if (hb->top_cap > 0) {
+                if ((e = cudaMemcpyAsync(hb->out_top_ids, c->h_top_ids.p, sizeof(int32_t) * (size_t)B * hb->top_cap,
+                                         cudaMemcpyDeviceToHost, st)) != cudaSuccess)
+                    break;
+                if ((e = cudaMemcpyAsync(hb->out_top_probs, c->h_top_probs.p, sizeof(float) * (size_t)B * hb->top_cap,
+                                         cudaMemcpyDeviceToHost, st)) != cudaSuccess)
+                    break;
+            }
+            e = cudaStreamSynchronize(st);
+        } while (0);
+        if (e != cudaSuccess) s = cuda_fail(c, e, "selection / copy back");
+        else s = read_status(c);
+    }
+    c->ctr.last_call_us =
+        std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
+    if (prev != c->device) cudaSetDevice(prev);
+    return s;
+}
+
+qsamp_status qsamp_get_counters(const qsamp_ctx* c, qsamp_counters* out) {
+    if (!c || !out) return QSAMP_ERR_INVALID_ARG;
+    *out = c->ctr;
+    return QSAMP_OK;
+}
+
+// ---------------------------------------------------------------- masks
+qsamp_status qsamp_pack_ids(const int32_t* ids, int64_t n, int32_t V, uint32_t* mask_out) {
+    if (V < 1 || !mask_out || (n > 0 && !ids) || n < 0) return QSAMP_ERR_INVALID_ARG;
+    const int64_t words = (V + 31) / 32;
+    std::memset(mask_out, 0, sizeof(uint32_t) * (size_t)words);
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t id = ids[i];
+        if (id >= 0 && id < V) mask_out[id >> 5] |= 1u << (id & 31);
+    }
+    return QSAMP_OK;
+}
+
+qsamp_status qsamp_grammar_mask(const int32_t* valid_ids, int64_t n_valid, int32_t accepting, int32_t eos_string_id,
+                                int32_t eos_token_id, int32_t V, uint32_t* mask_out, int32_t* force_token_out) {
+    if (V < 1 || !mask_out || !force_token_out || n_valid < 0 || (n_valid > 0 && !valid_ids))
+        return QSAMP_ERR_INVALID_ARG;
+    const int64_t words = (V + 31) / 32;
+    std::memset(mask_out, 0, sizeof(uint32_t) * (size_t)words);
+    *force_token_out = -1;
+    if (n_valid == 0) {
+        // stuck grammar: every logit -inf except the first EOS string's (0.0)
+        *force_token_out = (eos_string_id >= 0 && eos_string_id < V) ? eos_string_id : -1;
+        return QSAMP_OK;
+    }
+    for (int64_t i = 0; i < n_valid; ++i) {
+        const int32_t id = valid_ids[i];
+        if (id >= 0 && id < V) mask_out[id >> 5] |= 1u << (id & 31);
+    }
+    if (accepting) {
+        if (eos_string_id >= 0 && eos_string_id < V) mask_out[eos_string_id >> 5] |= 1u << (eos_string_id & 31);
+        if (eos_token_id >= 0 && eos_token_id < V) mask_out[eos_token_id >> 5] |= 1u << (eos_token_id & 31);
+    }
+    return QSAMP_OK;
+}
+
+int32_t qsamp_find_eos_string(const char* const* strs, const int32_t* lens, int32_t V) {
+    if (!strs || !lens) return -1;
+    static const char a[] = "<|endoftext|>", b[] = "<|im_end|>";
+    for (int32_t i = 0; i < V; ++i) {
+        const int32_t n = lens[i];
+        if (!strs[i]) continue;
+        if ((n == (int32_t)sizeof(a) - 1 && std::memcmp(strs[i], a, (size_t)n) == 0) ||
+            (n == (int32_t)sizeof(b) - 1 && std::memcmp(strs[i], b, (size_t)n) == 0))
+            return i;
+    }
+    return -1;
+}
+
+qsamp_status qsamp_keep_list_mask(const char* path, int32_t V, uint32_t* mask_out) {
+    if (!path || V < 1 || !mask_out) return QSAMP_ERR_INVALID_ARG;
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return QSAMP_ERR_IO;
+    uint32_t count = 0;
+    if (std::fread(&count, sizeof count, 1, f) != 1) {
+        std::fclose(f);
+        return QSAMP_ERR_IO;
+    }
+    const int64_t words = (V + 31) / 32;
+    std::memset(mask_out, 0, sizeof(uint32_t) * (size_t)words);
+    for (uint32_t i = 0; i < count; ++i) {
+        uint32_t id = 0;
+        if (std::fread(&id, sizeof id, 1, f) != 1) {
+            std::fclose(f);
+            return QSAMP_ERR_IO;
+        }
+        const int32_t sid = (int32_t)id;
+        if (sid >= 0 && sid < V) mask_out[sid >> 5] |= 1u << (sid & 31);
+    }
+    std::fclose(f);
+    return QSAMP_OK;
+}
+
+qsamp_status qsamp_mask_and(const uint32_t* a, const uint32_t* b, int64_t words, uint32_t* out) {
+    if (!a || !b || !out || words < 0) return QSAMP_ERR_INVALID_ARG;
+    for (int64_t i = 0; i < words; ++i) out[i] = a[i] & b[i];
+    return QSAMP_OK;
+}
+
+// ---------------------------------------------------------------- sharded
+qsamp_status qsamp_shard_topk(qsamp_ctx* c, const qsamp_batch* lb, int32_t v_offset, int32_t V_total, int32_t k,
+                              float* cand_vals, int32_t* cand_ids, void* stream) {
+    (void)lb; (void)v_offset; (void)V_total; (void)k; (void)cand_vals; (void)cand_ids; (void)stream;
+    return fail(c, QSAMP_ERR_UNSUPPORTED, "vocab-sharded selection is not built yet");
+}
+
+qsamp_status qsamp_merge_topk(qsamp_ctx* c, int32_t n_ranks, int32_t B, int32_t k, const float* all_vals,
+                              const int32_t* all_ids, const qsamp_row_params* params, const double* u,
+                              uint64_t rng_offset, int32_t* out_ids, qsamp_row_result* out_results, void* stream) {
+    (void)n_ranks; (void)B; (void)k; (void)all_vals; (void)all_ids; (void)params; (void)u; (void)rng_offset;
+    (void)out_ids; (void)out_results; (void)stream;
+    return fail(c, QSAMP_ERR_UNSUPPORTED, "vocab-sharded selection is not built yet");
+}
+
+}  // extern "C"

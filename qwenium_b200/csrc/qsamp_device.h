@@ -1,0 +1,118 @@
+// qsamp_device.h -- structures shared by the host API (qsamp_api.cu) and the
+// selection kernels (qsamp_kernels.cu). Internal; the public C ABI is
+// include/qsamp.h.
+#ifndef QSAMP_DEVICE_H
+#define QSAMP_DEVICE_H
+
+#include <stdint.h>
+
+#include "../../include/qsamp.h"
+
+namespace qs {
+
+constexpr int NT = 512;            // threads per CTA
+constexpr int NWARPS = NT / 32;
+constexpr int NB = 2048;           // value bins over x = l - max (bin NB-1 = tail)
+constexpr float BIN_R = 112.0f;    // bins per nat: bin(x) = min(NB-1, (int)(-x * BIN_R))
+constexpr int HIST_MAX = 4096;     // longest penalty window handled on the device
+constexpr int SPEC_CAP = 4096;     // elements gathered in sorted order per round
+constexpr int KMAX = 1024;         // largest top-k served by the sorted-candidate path
+constexpr int MAX_LUT = 4;         // distinct soft-cap values per call with bf16 tables
+constexpr int MAX_CLUSTER = 16;
+
+// Device status codes (first error wins; written with atomicCAS).
+enum DevStatus : int {
+    DEV_OK = 0,
+    DEV_TOPK_TOO_LARGE = 1,        // 0 < k < V with k > KMAX
+    DEV_ROUNDS_EXHAUSTED = 2,      // the exact walk needed more gather rounds than allowed
+    DEV_INTERNAL = 3,
+};
+
+struct QsLaunch {
+    const void* logits;
+    int dtype;                     // QSAMP_F32 / QSAMP_BF16
+    int B, V;
+    long long row_stride;          // elements
+    int vec_ok;                    // rows are 16-byte aligned: vector loads allowed
+    const qsamp_row_params* params;  // device [B]
+    const int32_t* hist;           // device [B][hist_stride] or null
+    int hist_stride;
+    const int32_t* hist_len;       // device [B] or null
+    const uint32_t* masks;         // device or null
+    long long mask_stride;         // words per row; 0 = shared
+    const double* u;               // device [B] or null (then Philox)
+    unsigned long long philox_offset;
+    const float* luts;             // device [MAX_LUT][65536]
+    float lut_caps[MAX_LUT];       // cap of each table; 0 = empty slot
+    qsamp_row_result* results;     // device [B]
+    int32_t* out_ids;              // device [B] or null
+    int32_t* top_ids;              // device [B][top_cap] or null
+    float* top_probs;              // device [B][top_cap] or null
+    int top_cap;
+    int* status;                   // device word
+    int n_s;                       // slice length per CTA (multiple of 8)
+    int max_rounds;                // gather rounds allowed per row
+};
+
+// Dynamic shared-memory layout; identical on host (sizing) and device.
+struct SmemLayout {
+    int off_vals, off_cnt, off_tsum, off_ksum, off_tx, off_sstart, off_flag, off_gs, off_gc, off_tie,
+        off_hist, off_spec, off_spect, off_misc, total;
+};
+
+// Per-CTA scalars kept at off_misc.
+struct __align__(16) Misc {
+    qsamp_row_params prm;
+    float red_f[NWARPS];
+    int red_i[NWARPS];
+    unsigned long long red_u[NWARPS];
+    float cmax;            // this CTA's slice max
+    int cmax_idx;
+    float M;               // row max
+    int argmax;
+    int cmd;               // command for this CTA (written by CTA 0)
+    int spec_n;            // CTA 0: gathered elements this round
+    int eq_count;          // elements equal to the selection key in this slice
+    int sel_bin;           // broadcast radix bin
+    int sel_rem;           // broadcast remaining rank
+    unsigned long long sel_remw;  // broadcast remaining weight (weighted select)
+    float S_n, S_c;        // exact sums (broadcast)
+    int first_round;
+    int round;
+    int ninf;              // -inf elements in this slice (full path)
+    int kmode, kfrom, kto; // integer sums to compute in this pass: 1 = S, 2 = top-p
+    int neg_quota;         // lowest-id -inf elements to gather (row total)
+    int n_sel;             // survivors cap: min(top_k, V) or V
+    int cum_bmax;          // last bin whose cum k-sums are needed
+    int tail_mode;         // weighted select restricted to the tail bin
+    float tail_x;          // tail threshold on x
+    uint32_t sel_prefix, sel_mask;
+    uint32_t gather_bits[NB / 32];
+};
+
+__host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+__host__ __device__ inline SmemLayout smem_layout(int n_s) {
+    SmemLayout L;
+    int o = 0;
+    L.off_vals = o;   o = align_up(o + n_s * 4, 16);
+    L.off_cnt = o;    o = align_up(o + NB * 4, 16);
+    L.off_tsum = o;   o = align_up(o + NB * 4, 16);     // float prediction sums
+    L.off_ksum = o;   o = align_up(o + NB * 8, 16);     // u64 quantised sums
+    L.off_tx = o;     o = align_up(o + NB * 8, 16);     // u64 fixed-point exact t sums (2^-40)
+    L.off_sstart = o; o = align_up(o + NB * 4, 16);     // float S at bin start
+    L.off_flag = o;   o = align_up(o + NB, 16);
+    L.off_gs = o;     o = align_up(o + NB, 16);
+    L.off_gc = o;     o = align_up(o + NB, 16);
+    L.off_tie = o;    o = align_up(o + NB / 8, 16);
+    L.off_hist = o;   o = align_up(o + HIST_MAX * 4, 16);
+    L.off_spec = o;   o = align_up(o + SPEC_CAP * 8, 16);
+    L.off_spect = o;  o = align_up(o + SPEC_CAP * 4, 16);
+    L.off_misc = o;   o = align_up(o + (int)sizeof(Misc), 16);
+    L.total = o;
+    return L;
+}
+
+}  // namespace qs
+
+#endif

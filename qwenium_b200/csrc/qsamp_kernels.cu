@@ -1,0 +1,1749 @@
+// qsamp_kernels.cu -- sm_100a token-selection kernels.
+//
+// One thread-block cluster (CL CTAs, CL in {2,4,8,16}) owns one row at a
+// time; CTA r holds logits [r*n_s, (r+1)*n_s) of the row in shared memory,
+// so the row is read from HBM exactly once. Clusters loop over rows.
+//
+// Row pipeline (the reference's order, src/sampling/sampling.cpp:137-194):
+//   transform (soft-cap, allow-mask, /T) -> penalty fix-up of the window ids
+//   -> row max -> greedy | top-k (k <= 1024) | full vocabulary.
+//
+// Exactness. The reference sums expf terms in float, sequentially, in sorted
+// order (sampling.cpp:171-177,184-188). Those sums are reproduced bit for
+// bit without sorting the vocabulary: while the running float sum S stays in
+// one binade [2^e, 2^(e+1)), S + t rounds to S + rne(t / ulp) * ulp, so the
+// contribution of a run of terms is an integer sum that does not depend on
+// their order. Terms are grouped into value bins over x = l - max; a bin
+// whose whole run provably stays in one binade, holds no rounding tie and
+// (for the top-p sum) does not reach top_p contributes its integer sum; the
+// few other bins are gathered, sorted, and walked element by element (32
+// lanes at a time with the same identity, a real float add wherever it does
+// not apply). Every step is verified during the walk; a wrong prediction
+// costs one more gather round, never a wrong result.
+#include <cooperative_groups.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "qs_math.h"
+#include "qsamp_device.h"
+
+namespace cg = cooperative_groups;
+
+namespace qs {
+
+#define FULLMASK 0xffffffffu
+
+enum Cmd : int { CMD_DONE = 0, CMD_PASS = 1 };
+enum BinFlag : uint8_t { F_GATH = 1, F_PLAINS = 2, F_PLAINC = 4, F_WANT = 8 };
+enum Stage : int { ST_SWALK = 0, ST_CUMPREP = 1, ST_CUMWALK = 2, ST_DRAW = 3, ST_FINISH = 4 };
+
+struct Sm {
+    float* vals;
+    uint32_t* cnt;
+    float* tsum;
+    uint32_t* specoff;   // aliases tsum after the predictions are made
+    unsigned long long* ksum;
+    double* pref;        // aliases ksum while predicting
+    unsigned long long* tx;
+    float* sstart;
+    uint8_t* flag;
+    int8_t* gs;
+    int8_t* gc;
+    uint32_t* tie;
+    int32_t* hist;
+    unsigned long long* spec;
+    float* spect;
+    Misc* misc;
+};
+
+__device__ __forceinline__ Sm carve(unsigned char* base, int n_s) {
+    const SmemLayout L = smem_layout(n_s);
+    Sm s;
+    s.vals = (float*)(base + L.off_vals);
+    s.cnt = (uint32_t*)(base + L.off_cnt);
+    s.tsum = (float*)(base + L.off_tsum);
+    s.specoff = (uint32_t*)(base + L.off_tsum);
+    s.ksum = (unsigned long long*)(base + L.off_ksum);
+    s.pref = (double*)(base + L.off_ksum);
+    s.tx = (unsigned long long*)(base + L.off_tx);
+    s.sstart = (float*)(base + L.off_sstart);
+    s.flag = (uint8_t*)(base + L.off_flag);
+    s.gs = (int8_t*)(base + L.off_gs);
+    s.gc = (int8_t*)(base + L.off_gc);
+    s.tie = (uint32_t*)(base + L.off_tie);
+    s.hist = (int32_t*)(base + L.off_hist);
+    s.spec = (unsigned long long*)(base + L.off_spec);
+    s.spect = (float*)(base + L.off_spect);
+    s.misc = (Misc*)(base + L.off_misc);
+    return s;
+}
+
+template <typename T>
+__device__ __forceinline__ T* peer(cg::cluster_group& cl, T* p, int rank) {
+    return cl.map_shared_rank(p, rank);
+}
+
+__device__ __forceinline__ void set_status(int* status, int code) {
+    if (status) atomicCAS(status, DEV_OK, code);
+}
+
+// NaN -> -inf (outside the reference's contract), -0 -> +0 (equal under the
+// reference's comparisons; one key per value here).
+__device__ __forceinline__ float canon(float v) {
+    if (v != v) return -__int_as_float(0x7f800000);
+    return v == 0.0f ? 0.0f : v;
+}
+
+__device__ __forceinline__ int binof(float x) {
+    // x <= 0; larger x -> lower bin. Monotone: rounding of -x*R preserves order.
+    // fmaxf maps a NaN x (an infinite logit, outside the contract) to bin 0.
+    const float y = fmaxf(__fmul_rn(-x, BIN_R), 0.0f);
+    return y >= (float)(NB - 1) ? NB - 1 : (int)y;
+}
+
+__device__ __forceinline__ int binade(float s) {  // s > 0, normal
+    return (int)(__float_as_uint(s) >> 23) - 127;
+}
+__device__ __forceinline__ float pow2f(int e) {  // 2^e, -126 <= e <= 127
+    return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+__device__ __forceinline__ int binade_d(double s) {  // floor(log2 s), s > 0
+    return (int)((__double_as_longlong(s) >> 52) & 0x7ff) - 1023;
+}
+
+__device__ __forceinline__ unsigned long long fixed40(float t) {  // t * 2^40, t <= 1
+    return (unsigned long long)__dmul_rn((double)t, 1099511627776.0);
+}
+
+__device__ __forceinline__ unsigned long long composite(float l, int idx) {
+    return ((unsigned long long)qs_key(l) << 32) | (uint32_t)(~(uint32_t)idx);
+}
+__device__ __forceinline__ float comp_val(unsigned long long c) { return qs_unkey((uint32_t)(c >> 32)); }
+__device__ __forceinline__ int comp_idx(unsigned long long c) { return (int)(~(uint32_t)c); }
+
+// ------------------------------------------------------------ block helpers
+__device__ float block_reduce_max_idx(float v, int idx, int& oidx, Misc* m) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_down_sync(FULLMASK, v, o);
+        const int i2 = __shfl_down_sync(FULLMASK, idx, o);
+        if (v2 > v || (v2 == v && i2 < idx)) { v = v2; idx = i2; }
+    }
+    __syncthreads();
+    if (lane == 0) { m->red_f[w] = v; m->red_i[w] = idx; }
+    __syncthreads();
+    if (w == 0) {
+        v = lane < NWARPS ? m->red_f[lane] : -__int_as_float(0x7f800000);
+        idx = lane < NWARPS ? m->red_i[lane] : 0x7fffffff;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float v2 = __shfl_down_sync(FULLMASK, v, o);
+            const int i2 = __shfl_down_sync(FULLMASK, idx, o);
+            if (v2 > v || (v2 == v && i2 < idx)) { v = v2; idx = i2; }
+        }
+        if (lane == 0) { m->red_f[0] = v; m->red_i[0] = idx; }
+    }
+    __syncthreads();
+    oidx = m->red_i[0];
+    return m->red_f[0];
+}
+
+__device__ int block_sum_int(int v, Misc* m) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(FULLMASK, v, o);
+    __syncthreads();
+    if (lane == 0) m->red_i[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        v = lane < NWARPS ? m->red_i[lane] : 0;
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(FULLMASK, v, o);
+        if (lane == 0) m->red_i[0] = v;
+    }
+    __syncthreads();
+    const int r = m->red_i[0];
+    __syncthreads();
+    return r;
+}
+
+// Exclusive scan of one int per thread in thread order.
+__device__ int block_excl_scan_int(int v, int& total, Misc* m) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(FULLMASK, x, o);
+        if (lane >= o) x += y;
+    }
+    __syncthreads();
+    if (lane == 31) m->red_i[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int s = lane < NWARPS ? m->red_i[lane] : 0;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(FULLMASK, s, o);
+            if (lane >= o) s += y;
+        }
+        if (lane < NWARPS) m->red_i[lane] = s;
+    }
+    __syncthreads();
+    const int base = w > 0 ? m->red_i[w - 1] : 0;
+    total = m->red_i[NWARPS - 1];
+    __syncthreads();
+    return base + x - v;
+}
+
+// Bitonic sort of n (power of two) u64 keys, descending, by the whole block.
+__device__ void bitonic_desc(unsigned long long* a, int n) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += NT) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long x = a[i], y = a[ixj];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? (x < y) : (x > y)) { a[i] = y; a[ixj] = x; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ void bitonic_asc_i32(int32_t* a, int n) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += NT) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const int32_t x = a[i], y = a[ixj];
+                    const bool asc = (i & k) == 0;
+                    if (asc ? (x > y) : (x < y)) { a[i] = y; a[ixj] = x; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ __forceinline__ int next_pow2(int n) {
+    int p = 1;
+    while (p < n) p <<= 1;
+    return p;
+}
+
+// ------------------------------------------------------------ exact walks
+// One full warp emulates `for (i < n) { S = S + term(i); if (S >= stop) return i; }`
+// (float, round to nearest) for non-negative, non-increasing terms with
+// S >= every term already added. Returns the stopping index or n.
+template <typename TermF>
+__device__ int warp_walk_terms(float& S, int n, float stop, TermF term) {
+    const int lane = threadIdx.x & 31;
+    int i = 0;
+    while (i < n) {
+        if (!(S > 0.0f)) {
+            S = __fadd_rn(S, term(i));
+            if (S >= stop) return i;
+            ++i;
+            continue;
+        }
+        const int e = binade(S);
+        const float up = pow2f(23 - e), down = pow2f(e - 23);
+        const uint32_t m = (uint32_t)__fmul_rn(S, up);
+        const int idx = i + lane;
+        const float t = idx < n ? term(idx) : 0.0f;
+        const float y = __fmul_rn(t, up);
+        const bool tie = (y - floorf(y)) == 0.5f;
+        const bool inr = idx < n && y < 16777216.0f;
+        const uint32_t k = inr ? (uint32_t)rintf(y) : 0u;
+        uint32_t pre = k;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t v = __shfl_up_sync(FULLMASK, pre, o);
+            if (lane >= o) pre += v;
+        }
+        const uint32_t prev = pre - k;
+        const bool ok = inr && !tie && (m + prev < (1u << 24)) && (m + pre <= (1u << 24));
+        const float after = __fmul_rn((float)(m + pre), down);
+        const uint32_t okm = __ballot_sync(FULLMASK, ok);
+        const int L = (okm == FULLMASK) ? 32 : (__ffs(~okm) - 1);
+        const uint32_t below = L == 32 ? FULLMASK : ((1u << L) - 1u);
+        const uint32_t hitm = __ballot_sync(FULLMASK, ok && after >= stop) & below;
+        if (hitm) {
+            const int Ls = __ffs(hitm) - 1;
+            S = __shfl_sync(FULLMASK, after, Ls);
+            return i + Ls;
+        }
+        if (L > 0) {
+            S = __shfl_sync(FULLMASK, after, L - 1);
+            i += L;
+        }
+        if (L < 32 && i < n) {
+            S = __fadd_rn(S, term(i));
+            if (S >= stop) return i;
+            ++i;
+        }
+    }
+    return n;
+}
+
+// One full warp advances S over bins [b, bend) whose k-sums (at binade g[b])
+// are valid for the current S; stops at the first bin that needs its
+// elements (returned), or at bend. Optionally records S at each bin start.
+__device__ int warp_walk_bins(float& S, int b, int bend, const Sm& s, const int8_t* g, uint8_t plain_bit,
+                              float stop, bool record) {
+    const int lane = threadIdx.x & 31;
+    while (b < bend) {
+        if (!(S > 0.0f)) {
+            // an empty bin before the first element leaves S at 0
+            const int bb = b + lane;
+            const bool empty = bb < bend && s.cnt[bb] == 0;
+            const uint32_t em = __ballot_sync(FULLMASK, empty);
+            const int L = (em == FULLMASK) ? 32 : (__ffs(~em) - 1);
+            if (record && lane < L && bb < bend) s.sstart[bb] = S;
+            b += L;
+            if (L < 32) return b < bend ? b : bend;
+            continue;
+        }
+        const int e = binade(S);
+        const float down = pow2f(e - 23);
+        const uint32_t m = (uint32_t)__fmul_rn(S, pow2f(23 - e));
+        const int bb = b + lane;
+        bool plain = false;
+        unsigned long long k = 0;
+        if (bb < bend) {
+            const uint32_t c = s.cnt[bb];
+            if (c == 0) {
+                plain = true;
+            } else {
+                const bool tied = (s.tie[bb >> 5] >> (bb & 31)) & 1u;
+                plain = (s.flag[bb] & plain_bit) && !(s.flag[bb] & F_GATH) && g[bb] == e && !tied;
+                if (plain) k = s.ksum[bb];
+            }
+        }
+        unsigned long long pre = k;
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long v = __shfl_up_sync(FULLMASK, pre, o);
+            if (lane >= o) pre += v;
+        }
+        const unsigned long long prev = pre - k;
+        const unsigned long long lim = 1ull << 24;
+        const float before = (m + prev <= lim) ? __fmul_rn((float)(m + prev), down) : 0.0f;
+        const float after = (m + pre <= lim) ? __fmul_rn((float)(m + pre), down) : 0.0f;
+        const bool ok = bb < bend && plain && (m + prev < lim) && (m + pre <= lim) && !(after >= stop);
+        const uint32_t okm = __ballot_sync(FULLMASK, ok);
+        const int L = (okm == FULLMASK) ? 32 : (__ffs(~okm) - 1);
+        if (record && lane <= L && bb < bend) s.sstart[bb] = before;
+        if (L > 0) S = __shfl_sync(FULLMASK, after, L - 1);
+        b += L;
+        if (L < 32) return b < bend ? b : bend;
+    }
+    return bend;
+}
+
+// ------------------------------------------------------------ row transform
+struct RowCtx {
+    const qsamp_row_params* p;
+    int row, V, lo, hi, len;
+    const void* rowp;
+    int dtype;
+    const float* lut;
+    bool cap_on, div_on, force_on;
+    int force;
+    float T, cap;
+    const uint32_t* mask;
+};
+
+__device__ __forceinline__ float raw_at(const RowCtx& r, int i) {
+    if (r.dtype == QSAMP_BF16) return qs_bf16_to_f32(((const uint16_t*)r.rowp)[i]);
+    return ((const float*)r.rowp)[i];
+}
+
+// soft-cap, then force/mask: the value the penalties see.
+__device__ __forceinline__ float pre_value(const RowCtx& r, int i, float raw, uint32_t bits16) {
+    if (r.force_on) return i == r.force ? 0.0f : -__int_as_float(0x7f800000);
+    float v = raw;
+    if (r.cap_on) v = r.lut ? r.lut[bits16] : qs_softcap(raw, r.cap);
+    if (r.mask && !((r.mask[i >> 5] >> (i & 31)) & 1u)) v = -__int_as_float(0x7f800000);
+    return v;
+}
+
+__device__ __forceinline__ float post_value(const RowCtx& r, float v) {
+    if (r.div_on) v = __fdiv_rn(v, r.T);
+    return canon(v);
+}
+
+__device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s) {
+    const int tid = threadIdx.x;
+    const int ngrp = r.len / 8;
+    const bool vec = a.vec_ok && !r.force_on;
+    if (vec) {
+        for (int g = tid; g < ngrp; g += NT) {
+            const int i0 = r.lo + 8 * g;
+            float x[8];
+            uint32_t b16[8];
+            if (r.dtype == QSAMP_BF16) {
+                const uint4 q = __ldg((const uint4*)((const uint16_t*)r.rowp + i0));
+                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    b16[2 * e] = w[e] & 0xffffu;
+                    b16[2 * e + 1] = w[e] >> 16;
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(b16[e] << 16);
+            } else {
+                const float4 p0 = __ldg((const float4*)((const float*)r.rowp + i0));
+                const float4 p1 = __ldg((const float4*)((const float*)r.rowp + i0 + 4));
+                x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
+                x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) b16[e] = 0;
+            }
+            const uint32_t mw = r.mask ? (r.mask[i0 >> 5] >> (i0 & 31)) : 0xffu;
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                float v = x[e];
+                if (r.cap_on) v = r.lut ? r.lut[b16[e]] : qs_softcap(v, r.cap);
+                if (!((mw >> e) & 1u)) v = -__int_as_float(0x7f800000);
+                o[e] = post_value(r, v);
+            }
+            float4* dst = (float4*)(s.vals + 8 * g);
+            dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+        }
+        for (int i = r.lo + 8 * ngrp + tid; i < r.hi; i += NT) {
+            const float raw = raw_at(r, i);
+            const uint32_t b16 = r.dtype == QSAMP_BF16 ? ((const uint16_t*)r.rowp)[i] : 0u;
+            s.vals[i - r.lo] = post_value(r, pre_value(r, i, raw, b16));
+        }
+    } else {
+        for (int i = r.lo + tid; i < r.hi; i += NT) {
+            const float raw = r.force_on ? 0.0f : raw_at(r, i);
+            const uint32_t b16 = (!r.force_on && r.dtype == QSAMP_BF16) ? ((const uint16_t*)r.rowp)[i] : 0u;
+            s.vals[i - r.lo] = post_value(r, pre_value(r, i, raw, b16));
+        }
+    }
+}
+
+// Penalties over the window (sampling.cpp:124-135 plus the frequency /
+// presence extension): every CTA sorts the window ids, and the leader of
+// each run that falls in this slice recomputes its value.
+__device__ void penalty_fixup(const RowCtx& r, const QsLaunch& a, const Sm& s) {
+    const qsamp_row_params& p = *r.p;
+    const bool rep_on = p.repetition_penalty != 1.0f;
+    const bool fp_on = p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
+    if (!(rep_on || fp_on) || !a.hist) return;
+    const int len = a.hist_len ? a.hist_len[r.row] : a.hist_stride;
+    if (len <= 0) return;
+    const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
+    const int w = (int)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
+    if (w <= 0) return;
+    const int start = len - w;
+    const int P2 = next_pow2(w);
+    const int32_t* h = a.hist + (size_t)r.row * (size_t)a.hist_stride + start;
+    for (int j = threadIdx.x; j < P2; j += NT) s.hist[j] = j < w ? h[j] : 0x7fffffff;
+    __syncthreads();
+    bitonic_asc_i32(s.hist, P2);
+    for (int j = threadIdx.x; j < w; j += NT) {
+        const int32_t id = s.hist[j];
+        if (j > 0 && s.hist[j - 1] == id) continue;
+        if (id < r.lo || id >= r.hi) continue;
+        int c = 1;
+        while (j + c < w && s.hist[j + c] == id) ++c;
+        const float raw = r.force_on ? 0.0f : raw_at(r, id);
+        const uint32_t b16 = (!r.force_on && r.dtype == QSAMP_BF16) ? ((const uint16_t*)r.rowp)[id] : 0u;
+        float v = pre_value(r, id, raw, b16);
+        if (rep_on) v = v < 0.0f ? __fmul_rn(v, p.repetition_penalty) : __fdiv_rn(v, p.repetition_penalty);
+        if (fp_on) {
+            v = __fsub_rn(v, __fmul_rn((float)c, p.frequency_penalty));
+            v = __fsub_rn(v, p.presence_penalty);
+        }
+        s.vals[id - r.lo] = post_value(r, v);
+    }
+    __syncthreads();
+}
+
+// ------------------------------------------------------------ outputs
+__device__ void write_result(const QsLaunch& a, int row, const qsamp_row_result& res) {
+    a.results[row] = res;
+    if (a.out_ids) a.out_ids[row] = res.token;
+}
+
+__device__ double philox_uniform(unsigned long long seed, unsigned long long counter, int row) {
+    // Philox4x32-10 (Salmon et al., SC'11), key = seed, counter = (row, offset).
+    uint32_t c0 = (uint32_t)row, c1 = 0u, c2 = (uint32_t)counter, c3 = (uint32_t)(counter >> 32);
+    uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t hi0 = __umulhi(0xD2511F53u, c0), lo0 = 0xD2511F53u * c0;
+        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c2), lo1 = 0xCD9E8D57u * c2;
+        const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+        c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    // u = (g1 + g2 * 2^32) / 2^64, as std::generate_canonical<double,53> forms it
+    const double sum = __dadd_rn((double)c0, __dmul_rn((double)c1, 4294967296.0));
+    double u = __dmul_rn(sum, 5.421010862427522e-20);
+    if (u >= 1.0) u = 0x1.fffffffffffffp-1;
+    return u;
+}
+
+__device__ __forceinline__ double row_u(const QsLaunch& a, int row, const qsamp_row_params& p) {
+    return a.u ? a.u[row] : philox_uniform(p.seed, a.philox_offset, row);
+}
+
+// libstdc++ lower_bound over cp[0..n): first j with !(cp[j] < u).
+__device__ int lower_bound_d(const double* cp, int n, double u) {
+    int first = 0, len = n;
+    while (len > 0) {
+        const int half = len >> 1;
+        const int mid = first + half;
+        if (cp[mid] < u) {
+            first = mid + 1;
+            len = len - half - 1;
+        } else {
+            len = half;
+        }
+    }
+    return first;
+}
+
+// ------------------------------------------------------------ top-k path
+// Candidates (k <= KMAX) sorted in s.spec[0..k); CTA 0 finishes the row
+// exactly as sampling.cpp:168-193 does, on one thread where the reference
+// is sequential.
+__device__ void topk_tail(const QsLaunch& a, int row, int k, const Sm& s) {
+    Misc* m = s.misc;
+    const qsamp_row_params& p = m->prm;
+    const float M = m->M;
+    float* t = s.spect;              // [k]
+    float* part = s.sstart;          // partial sums after i+1 terms [k] (k <= NB)
+    float* prob = s.tsum;            // [k]
+    double* cp = s.pref;             // [k] (k <= NB)
+    for (int i = threadIdx.x; i < k; i += NT) t[i] = qs_expf(__fsub_rn(comp_val(s.spec[i]), M));
+    __syncthreads();
+    const bool pa = p.top_p > 0.0f && p.top_p < 1.0f;
+    if (threadIdx.x == 0) {
+        float S = 0.0f;
+        for (int i = 0; i < k; ++i) {
+            S = __fadd_rn(S, t[i]);
+            part[i] = S;
+        }
+        int c = k;
+        if (pa) {
+            float cum = 0.0f;
+            for (int i = 0; i < k; ++i) {
+                cum = __fadd_rn(cum, __fdiv_rn(t[i], S));
+                if (cum >= p.top_p) {
+                    c = i + 1;
+                    break;
+                }
+            }
+        }
+        m->S_n = pa ? S : 0.0f;
+        m->S_c = part[c - 1];
+        m->spec_n = c;
+    }
+    __syncthreads();
+    const int c = m->spec_n;
+    const float Sc = m->S_c;
+    for (int i = threadIdx.x; i < c; i += NT) prob[i] = __fdiv_rn(t[i], Sc);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int j = 0, drew = 0;
+        if (c >= 2) {
+            double dsum = 0.0;
+            for (int i = 0; i < c; ++i) dsum = __dadd_rn(dsum, (double)prob[i]);
+            double acc = 0.0;
+            for (int i = 0; i < c; ++i) {
+                acc = __dadd_rn(acc, __ddiv_rn((double)prob[i], dsum));
+                cp[i] = acc;
+            }
+            cp[c - 1] = 1.0;
+            j = lower_bound_d(cp, c, row_u(a, row, p));
+            drew = 1;
+        }
+        qsamp_row_result res;
+        res.token = comp_idx(s.spec[j]);
+        res.position = j;
+        res.n_keep = c;
+        res.drew = drew;
+        res.sum_exp = m->S_n;
+        res.sum_keep = Sc;
+        res.max_logit = M;
+        res.prob = prob[j];
+        write_result(a, row, res);
+    }
+    if (a.top_ids) {
+        for (int i = threadIdx.x; i < a.top_cap; i += NT) {
+            a.top_ids[(size_t)row * a.top_cap + i] = i < c ? comp_idx(s.spec[i]) : -1;
+            a.top_probs[(size_t)row * a.top_cap + i] = i < c ? prob[i] : 0.0f;
+        }
+    }
+    __syncthreads();
+}
+
+// Exact k-th largest key over the cluster (3 radix rounds of 11/11/10
+// bits); returns the key and how many elements equal to it belong to the
+// top k (the lowest ids first).
+__device__ uint32_t cluster_radix_select(cg::cluster_group& cl, const RowCtx& r, const Sm& s, int k, int& need) {
+    Misc* m = s.misc;
+    const int rank = cl.block_rank(), CL = cl.num_blocks();
+    uint32_t prefix = 0, pmask = 0;
+    int rem = k;
+    for (int round = 0; round < 3; ++round) {
+        const int shift = round == 0 ? 21 : (round == 1 ? 10 : 0);
+        const int nbins = round == 2 ? 1024 : 2048;
+        for (int b = threadIdx.x; b < nbins; b += NT) s.cnt[b] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < r.len; i += NT) {
+            const uint32_t key = qs_key(s.vals[i]);
+            if ((key & pmask) == prefix) atomicAdd(&s.cnt[(key >> shift) & (nbins - 1)], 1u);
+        }
+        __syncthreads();
+        cl.sync();
+        if (rank == 0) {
+            // totals into the upper half of cnt's neighbour (tsum region as u32)
+            uint32_t* tot = (uint32_t*)s.tsum;
+            for (int b = threadIdx.x; b < nbins; b += NT) {
+                uint32_t sum = 0;
+                for (int q = 0; q < CL; ++q) sum += peer(cl, s.cnt, q)[b];
+                tot[b] = sum;
+            }
+            __syncthreads();
+            if (threadIdx.x < 32) {
+                // walk bins from the top; find the one holding the rem-th largest
+                const int lane = threadIdx.x;
+                int acc = 0, found = -1, left = rem;
+                for (int base = nbins - 1; base >= 0 && found < 0; base -= 32) {
+                    const int b = base - lane;
+                    const int c = b >= 0 ? (int)tot[b] : 0;
+                    int pre = c;
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int v = __shfl_up_sync(FULLMASK, pre, o);
+                        if (lane >= o) pre += v;
+                    }
+                    const bool hit = acc + pre >= rem;
+                    const uint32_t hm = __ballot_sync(FULLMASK, hit && b >= 0);
+                    if (hm) {
+                        const int L = __ffs(hm) - 1;
+                        const int preL = __shfl_sync(FULLMASK, pre, L);
+                        const int cL = __shfl_sync(FULLMASK, c, L);
+                        found = base - L;
+                        left = rem - (acc + preL - cL);
+                    } else {
+                        acc += __shfl_sync(FULLMASK, pre, 31);
+                    }
+                }
+                if (lane == 0) {
+                    for (int q = 0; q < CL; ++q) {
+                        peer(cl, &m->sel_bin, q)[0] = found < 0 ? 0 : found;
+                        peer(cl, &m->sel_rem, q)[0] = left;
+                    }
+                }
+            }
+        }
+        cl.sync();
+        prefix |= (uint32_t)m->sel_bin << shift;
+        pmask |= (uint32_t)(nbins - 1) << shift;
+        rem = m->sel_rem;
+    }
+    need = rem;
+    return prefix;
+}
+
+__device__ void append_to_leader(cg::cluster_group& cl, const Sm& s, bool want, unsigned long long comp) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t wm = __ballot_sync(FULLMASK, want);
+    if (!wm) return;
+    int base = 0;
+    if (lane == __ffs(wm) - 1) base = atomicAdd(peer(cl, &s.misc->spec_n, 0), __popc(wm));
+    base = __shfl_sync(FULLMASK, base, __ffs(wm) - 1);
+    if (want) {
+        const int slot = base + __popc(wm & ((1u << lane) - 1u));
+        if (slot < SPEC_CAP) peer(cl, s.spec, 0)[slot] = comp;
+    }
+}
+
+__device__ void topk_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch& a, const Sm& s, int k) {
+    Misc* m = s.misc;
+    const int rank = cl.block_rank(), CL = cl.num_blocks();
+    int need = 0;
+    const uint32_t K = cluster_radix_select(cl, r, s, k, need);
+    // elements equal to K per CTA -> this CTA's quota of them (lowest ids first)
+    int eq = 0;
+    for (int i = threadIdx.x; i < r.len; i += NT) eq += qs_key(s.vals[i]) == K;
+    eq = block_sum_int(eq, m);
+    if (threadIdx.x == 0) {
+        m->eq_count = eq;
+        if (rank == 0) m->spec_n = 0;
+    }
+    __syncthreads();
+    cl.sync();
+    int before = 0;
+    for (int q = 0; q < rank; ++q) before += peer(cl, &m->eq_count, q)[0];
+    int quota = need - before;
+    quota = quota < 0 ? 0 : (quota > eq ? eq : quota);
+    // strictly greater: all; equal: the first `quota` in id order
+    const int rounds = (r.len + NT - 1) / NT;
+    for (int it = 0; it < rounds; ++it) {
+        const int i = it * NT + threadIdx.x;
+        const float v = i < r.len ? s.vals[i] : 0.0f;
+        const uint32_t key = i < r.len ? qs_key(v) : 0u;
+        append_to_leader(cl, s, i < r.len && key > K, composite(v, r.lo + i));
+    }
+    if (quota == eq) {
+        for (int it = 0; it < rounds; ++it) {
+            const int i = it * NT + threadIdx.x;
+            const float v = i < r.len ? s.vals[i] : 0.0f;
+            append_to_leader(cl, s, i < r.len && qs_key(v) == K, composite(v, r.lo + i));
+        }
+    } else if (quota > 0) {
+        // ordered: chunks of NT consecutive elements, ranks by a block scan
+        int taken = 0;
+        for (int base = 0; base < r.len && taken < quota; base += NT) {
+            const int i = base + threadIdx.x;
+            const float v = i < r.len ? s.vals[i] : 0.0f;
+            const bool isq = i < r.len && qs_key(v) == K;
+            int tot = 0;
+            const int rk = block_excl_scan_int(isq ? 1 : 0, tot, m);
+            append_to_leader(cl, s, isq && taken + rk < quota, composite(v, r.lo + i));
+            taken += tot;
+        }
+    }
+    __syncthreads();
+    cl.sync();
+    if (rank == 0) {
+        const int P2 = next_pow2(k);
+        for (int i = k + threadIdx.x; i < P2; i += NT) s.spec[i] = 0ull;
+        __syncthreads();
+        bitonic_desc(s.spec, P2);
+        topk_tail(a, r.row, k, s);
+    }
+}
+
+// ------------------------------------------------------------ full path
+__device__ void push_flags(cg::cluster_group& cl, const Sm& s) {
+    // CTA 0 copies flag / gs / gc / scalars to every other CTA
+    const int CL = cl.num_blocks();
+    for (int q = 1; q < CL; ++q) {
+        uint32_t* df = (uint32_t*)peer(cl, s.flag, q);
+        uint32_t* dgs = (uint32_t*)peer(cl, (uint8_t*)s.gs, q);
+        uint32_t* dgc = (uint32_t*)peer(cl, (uint8_t*)s.gc, q);
+        const uint32_t* sf = (const uint32_t*)s.flag;
+        const uint32_t* sgs = (const uint32_t*)s.gs;
+        const uint32_t* sgc = (const uint32_t*)s.gc;
+        for (int w = threadIdx.x; w < NB / 4; w += NT) {
+            df[w] = sf[w];
+            dgs[w] = sgs[w];
+            dgc[w] = sgc[w];
+        }
+        if (threadIdx.x == 0) {
+            Misc* pm = peer(cl, s.misc, q);
+            pm->cmd = s.misc->cmd;
+            pm->first_round = s.misc->first_round;
+            pm->S_n = s.misc->S_n;
+            pm->cum_bmax = s.misc->cum_bmax;
+            pm->neg_quota = s.misc->neg_quota;
+            pm->kmode = s.misc->kmode;
+            pm->kfrom = s.misc->kfrom;
+            pm->kto = s.misc->kto;
+        }
+    }
+}
+
+// Exclusive prefix over bins of a per-bin value, by the whole CTA (NB = 4*NT).
+template <typename T, typename F>
+__device__ T block_bin_prefix(F get, T* out, Misc* m, T* total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int b0 = threadIdx.x * (NB / NT);
+    T v[NB / NT];
+    T run = T(0);
+#pragma unroll
+    for (int j = 0; j < NB / NT; ++j) {
+        v[j] = get(b0 + j);
+        run = run + v[j];
+    }
+    T x = run;
+    for (int o = 1; o < 32; o <<= 1) {
+        const T y = __shfl_up_sync(FULLMASK, x, o);
+        if (lane >= o) x = x + y;
+    }
+    __shared__ T wsum[NWARPS];
+    __syncthreads();
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    T base = T(0);
+    for (int q = 0; q < w; ++q) base = base + wsum[q];
+    T acc = base + x - run;
+#pragma unroll
+    for (int j = 0; j < NB / NT; ++j) {
+        out[b0 + j] = acc;
+        acc = acc + v[j];
+    }
+    T tot = T(0);
+    for (int q = 0; q < NWARPS; ++q) tot = tot + wsum[q];
+    if (total) *total = tot;
+    __syncthreads();
+    return tot;
+}
+
+// Bins to gather (sorted) in the next pass: `first` (if >= 0), then wanted
+// bins in bin order while the list (plus the -inf quota) fits SPEC_CAP.
+// Sets F_GATH, the list offset of every gathered bin, and the pass command.
+__device__ void build_gather_set(const Sm& s, int first, bool& overflow) {
+    Misc* m = s.misc;
+    __shared__ int bgs_used0, bgs_ovf;
+    if (threadIdx.x == 0) {
+        const int c0 = first >= 0 ? (int)s.cnt[first] : 0;
+        bgs_used0 = m->neg_quota + c0;
+        bgs_ovf = bgs_used0 > SPEC_CAP;
+    }
+    __syncthreads();
+    uint32_t* pre = (uint32_t*)s.spect;  // scratch: the sorted list is rebuilt by the pass
+    // wanted counts in bin order (excluding `first`)
+    block_bin_prefix<uint32_t>([&](int b) {
+        return (b != first && (s.flag[b] & F_WANT) && s.cnt[b] > 0) ? s.cnt[b] : 0u;
+    }, pre, m, (uint32_t*)nullptr);
+    const int used0 = bgs_used0;
+    for (int b = threadIdx.x; b < NB; b += NT) {
+        const bool cand = b != first && (s.flag[b] & F_WANT) && s.cnt[b] > 0;
+        const bool take = (b == first && !bgs_ovf) || (cand && used0 + (int)pre[b] + (int)s.cnt[b] <= SPEC_CAP);
+        s.flag[b] = take ? (uint8_t)(s.flag[b] | F_GATH) : (uint8_t)(s.flag[b] & ~F_GATH);
+    }
+    __syncthreads();
+    block_bin_prefix<uint32_t>([&](int b) { return (s.flag[b] & F_GATH) ? s.cnt[b] : 0u; }, s.specoff, m,
+                               (uint32_t*)nullptr);
+    if (threadIdx.x == 0) {
+        overflow = bgs_ovf != 0;
+        m->spec_n = 0;
+        m->cmd = CMD_PASS;
+        m->round += 1;
+    }
+    __syncthreads();
+    overflow = bgs_ovf != 0;
+}
+
+// Keep only the top k elements (value desc, id asc) of the row: everything
+// else becomes -inf. Used for k above the sorted-candidate limit, followed
+// by the full-vocabulary path over the survivors (sampling.cpp:165-166).
+__device__ void restrict_to_topk(cg::cluster_group& cl, const RowCtx& r, const Sm& s, int k) {
+    Misc* m = s.misc;
+    const int rank = cl.block_rank();
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    int need = 0;
+    const uint32_t K = cluster_radix_select(cl, r, s, k, need);
+    int eq = 0;
+    for (int i = threadIdx.x; i < r.len; i += NT) eq += qs_key(s.vals[i]) == K;
+    eq = block_sum_int(eq, m);
+    if (threadIdx.x == 0) m->eq_count = eq;
+    __syncthreads();
+    cl.sync();
+    int before = 0;
+    for (int q = 0; q < rank; ++q) before += peer(cl, &m->eq_count, q)[0];
+    int quota = need - before;
+    quota = quota < 0 ? 0 : (quota > eq ? eq : quota);
+    int taken = 0;
+    for (int base = 0; base < r.len; base += NT) {
+        const int i = base + threadIdx.x;
+        const uint32_t key = i < r.len ? qs_key(s.vals[i]) : 0u;
+        const bool isq = i < r.len && key == K;
+        int tot = 0;
+        const int rk = block_excl_scan_int(isq ? 1 : 0, tot, m);
+        if (i < r.len && (key < K || (isq && taken + rk >= quota))) s.vals[i] = NEG_INF;
+        taken += tot;
+    }
+    __syncthreads();
+    cl.sync();
+}
+
+// Persistent per-row state of CTA 0's walk state machine.
+struct WalkState {
+    int stage;
+    int swb;            // S walk: next bin
+    float S;            // S walk: running sum
+    int cwb;            // top-p walk: next bin
+    float C;            // top-p walk: running cum
+    int cut_all;        // 1: every element survives (no cutoff)
+    int cut_bin, cut_idx;
+    long long n_keep;
+    float Sc;
+    double mass_cut;    // sum of survivor probabilities inside cut_bin
+    long long draw_rank;
+    int draw_id;
+    float draw_prob;
+    int drew;
+    int need;           // bin to gather next, -1 none
+    int dbin;           // bin holding the drawn element
+    int big;            // draw by weighted selection instead of gathering
+    double acc, tgt;    // survivor mass before dbin, and u * total (probability units)
+};
+
+// CTA 0 alone: among the finite elements of x-bin `bsel` (order: value desc,
+// id asc), the element where the running sum of t first reaches R_t (t
+// units). Reads every CTA's slice through distributed shared memory, so the
+// bin never has to fit a gather list. Returns the id, how many elements of
+// the bin precede it, and its probability t / Sc.
+__device__ void leader_weighted_select(cg::cluster_group& cl, const Sm& s, int n_s, int V, int bsel, double R_t,
+                                       float M, float Sc, int& out_id, long long& out_before, float& out_prob) {
+    const int CL = cl.num_blocks();
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    unsigned long long* hw = s.ksum;
+    uint32_t* hc = (uint32_t*)s.sstart;
+    __shared__ uint32_t ws_prefix, ws_mask, ws_cntK;
+    __shared__ unsigned long long ws_R;
+    __shared__ long long ws_before;
+    __shared__ int ws_found[NWARPS], ws_id;
+    // fixed-point scale: the bin's mass is below cnt * expf(-bsel / R)
+    const float tmax = qs_expf(-(float)bsel / BIN_R);
+    const double bound = fmax((double)s.cnt[bsel] * (double)tmax, 1e-300);
+    int sc = 61 - binade_d(bound) - 1;
+    sc = sc < 0 ? 0 : (sc > 960 ? 960 : sc);
+    const double scale = ldexp(1.0, sc);
+    if (threadIdx.x == 0) {
+        ws_prefix = 0;
+        ws_mask = 0;
+        const double rf = fmax(R_t, 0.0) * scale;
+        ws_R = rf >= 0x1p62 ? (1ull << 62) : (unsigned long long)rf;
+        ws_before = 0;
+    }
+    __syncthreads();
+    for (int round = 0; round < 3; ++round) {
+        const int shift = round == 0 ? 21 : (round == 1 ? 10 : 0);
+        const int nbins = round == 2 ? 1024 : 2048;
+        for (int d = threadIdx.x; d < nbins; d += NT) { hw[d] = 0ull; hc[d] = 0u; }
+        __syncthreads();
+        const uint32_t prefix = ws_prefix, pmask = ws_mask;
+        for (int q = 0; q < CL; ++q) {
+            const float* pv = peer(cl, s.vals, q);
+            const int lo = q * n_s;
+            const int len = min(V, lo + n_s) - lo;
+            for (int i = threadIdx.x; i < len; i += NT) {
+                const float v = pv[i];
+                if (v == NEG_INF) continue;
+                const float x = __fsub_rn(v, M);
+                if (binof(x) != bsel) continue;
+                const uint32_t key = qs_key(v);
+                if ((key & pmask) != prefix) continue;
+                const int d = (key >> shift) & (nbins - 1);
+                atomicAdd(&hw[d], (unsigned long long)__dmul_rn((double)qs_expf(x), scale));
+                atomicAdd(&hc[d], 1u);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long R = ws_R, cum = 0;
+            long long cabove = 0;
+            int sel = -1, last = -1;
+            for (int d = nbins - 1; d >= 0; --d) {
+                if (hc[d] == 0) continue;
+                last = d;
+                if (cum + hw[d] >= R) { sel = d; break; }
+                cum += hw[d];
+                cabove += hc[d];
+            }
+            if (sel < 0) {  // the target lies past the bin's mass: its last element
+                sel = last < 0 ? 0 : last;
+                cabove -= last < 0 ? 0 : hc[last];
+                cum -= last < 0 ? 0 : hw[last];
+                R = cum + (last < 0 ? 0 : hw[last]);
+            }
+            ws_R = R - cum;
+            ws_before += cabove;
+            ws_prefix = prefix | ((uint32_t)sel << shift);
+            ws_mask = pmask | ((uint32_t)(nbins - 1) << shift);
+            ws_cntK = hc[sel];
+        }
+        __syncthreads();
+    }
+    // the pos-th lowest id among elements equal to K
+    const uint32_t K = ws_prefix;
+    const float tK = qs_expf(__fsub_rn(qs_unkey(K), M));
+    const unsigned long long wK = (unsigned long long)__dmul_rn((double)tK, scale);
+    long long pos = wK > 0 ? (long long)((ws_R + wK - 1) / wK) - 1 : 0;
+    if (pos < 0) pos = 0;
+    if (pos > (long long)ws_cntK - 1) pos = (long long)ws_cntK - 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int chunk = (V + NWARPS - 1) / NWARPS;
+    const int c0 = warp * chunk, c1 = min(V, c0 + chunk);
+    int mine = 0;
+    for (int id = c0 + lane; id < c1; id += 32) {
+        const float v = peer(cl, s.vals, id / n_s)[id % n_s];
+        mine += (v != NEG_INF && qs_key(v) == K) ? 1 : 0;
+    }
+    for (int o = 16; o > 0; o >>= 1) mine += __shfl_down_sync(FULLMASK, mine, o);
+    if (lane == 0) ws_found[warp] = mine;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        long long acc = 0;
+        int wsel = NWARPS - 1;
+        for (int q = 0; q < NWARPS; ++q) {
+            if (acc + ws_found[q] > pos) { wsel = q; break; }
+            acc += ws_found[q];
+        }
+        ws_found[0] = wsel;
+        ws_before += 0;
+        ws_id = (int)(pos - acc);  // rank inside the selected warp's chunk
+    }
+    __syncthreads();
+    if (warp == ws_found[0]) {
+        int want = ws_id, id_out = -1;
+        for (int base = c0; base < c1 && id_out < 0; base += 32) {
+            const int id = base + lane;
+            bool hit = false;
+            if (id < c1) {
+                const float v = peer(cl, s.vals, id / n_s)[id % n_s];
+                hit = v != NEG_INF && qs_key(v) == K;
+            }
+            const uint32_t bm = __ballot_sync(FULLMASK, hit);
+            const int n = __popc(bm);
+            if (want < n) {
+                uint32_t mm = bm;
+                for (int j = 0; j < want; ++j) mm &= mm - 1;
+                id_out = base + __ffs(mm) - 1;
+            } else {
+                want -= n;
+            }
+        }
+        if (lane == 0) ws_id = id_out;
+    }
+    __syncthreads();
+    out_id = ws_id;
+    out_before = ws_before + pos;
+    out_prob = __fdiv_rn(tK, Sc);
+    __syncthreads();
+}
+
+// CTA 0: S-walk predictions for bins >= from: the expected running sum at a
+// bin's start is the exact prefix of t (tx) scaled by `ratio` (the measured
+// float-sum / exact-sum ratio at `from`); bins whose run may leave a binade,
+// and `from` itself, are gathered, the rest get integer sums at the guessed
+// binade.
+__device__ void predict_s(const Sm& s, int from, double ratio) {
+    Misc* m = s.misc;
+    block_bin_prefix<double>([&](int b) { return b < NB - 1 ? (double)s.tx[b] * 0x1p-40 : 0.0; }, s.pref, m,
+                             (double*)nullptr);
+    const double D = 2e-3;
+    for (int b = threadIdx.x; b < NB; b += NT) {
+        uint8_t f = (uint8_t)(s.flag[b] & ~(F_PLAINS | F_WANT));
+        if (b >= from && b < NB - 1 && s.cnt[b] > 0) {
+            const double Pa = s.pref[b] * ratio, Pb = (s.pref[b] + (double)s.tx[b] * 0x1p-40) * ratio;
+            const bool want = b == from || !(Pa > 0.0) || binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
+            if (want) f |= F_WANT;
+            else { f |= F_PLAINS; s.gs[b] = (int8_t)binade_d(Pa); }
+        }
+        s.flag[b] = f;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        m->kmode = 1;
+        m->kfrom = from;
+        m->kto = NB - 2;
+    }
+    __syncthreads();
+}
+
+// CTA 0: top-p walk predictions for bins >= from (cum ~ prefix(t) / S_n,
+// scaled by `ratio`); bins at a binade change or near top_p are gathered.
+__device__ void predict_c(const Sm& s, int from, double ratio, float top_p) {
+    Misc* m = s.misc;
+    const double Sn = m->S_n;
+    block_bin_prefix<double>([&](int b) { return b < NB - 1 ? (double)s.tx[b] * 0x1p-40 : 0.0; }, s.pref, m,
+                             (double*)nullptr);
+    const double D = 2e-3, pp = top_p;
+    int bmax = -1;
+    for (int b = threadIdx.x; b < NB; b += NT) {
+        uint8_t f = (uint8_t)(s.flag[b] & ~(F_PLAINC | F_WANT));
+        if (b >= from && b < NB - 1 && s.cnt[b] > 0) {
+            const double ca = s.pref[b] / Sn * ratio, cb = (s.pref[b] + (double)s.tx[b] * 0x1p-40) / Sn * ratio;
+            if (ca <= pp + 1e-2) {
+                bmax = b > bmax ? b : bmax;
+                const bool crossing = !(ca > 0) || binade_d(ca * (1 - D)) != binade_d(cb * (1 + D));
+                const bool cut = cb >= pp - D && ca <= pp + D;
+                if (crossing || cut || b == from) f |= F_WANT;
+                else { f |= F_PLAINC; s.gc[b] = (int8_t)binade_d(ca); }
+            }
+        }
+        s.flag[b] = f;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const int y = __shfl_down_sync(FULLMASK, bmax, o);
+        bmax = y > bmax ? y : bmax;
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) m->red_i[threadIdx.x >> 5] = bmax;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int x = -1;
+        for (int q = 0; q < NWARPS; ++q) x = m->red_i[q] > x ? m->red_i[q] : x;
+        m->kmode = 2;
+        m->kfrom = from;
+        m->kto = x < 0 ? NB - 2 : x;
+    }
+    __syncthreads();
+}
+
+__device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch& a, const Sm& s) {
+    Misc* m = s.misc;
+    const qsamp_row_params& p = m->prm;
+    const int rank = cl.block_rank(), CL = cl.num_blocks();
+    const float M = m->M;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    const float POS_INF = __int_as_float(0x7f800000);
+    const bool pa = p.top_p > 0.0f && p.top_p < 1.0f;
+    const int NSEL = m->n_sel;  // survivors when no top-p cutoff applies
+    __shared__ WalkState w;
+    __shared__ long long n_finite;
+    const int lane = threadIdx.x & 31;
+
+    // F1: counts and approximate t sums per bin; the tail bin in registers
+    for (int b = threadIdx.x; b < NB; b += NT) { s.cnt[b] = 0; s.tsum[b] = 0.0f; }
+    __syncthreads();
+    int ninf = 0, ntail = 0;
+    for (int i = threadIdx.x; i < r.len; i += NT) {
+        const float v = s.vals[i];
+        if (v == NEG_INF) { ++ninf; continue; }
+        const float x = __fsub_rn(v, M);
+        const int b = binof(x);
+        if (b == NB - 1) { ++ntail; continue; }
+        atomicAdd(&s.cnt[b], 1u);
+        atomicAdd(&s.tsum[b], __expf(x));
+    }
+    for (int o = 16; o > 0; o >>= 1) ntail += __shfl_down_sync(FULLMASK, ntail, o);
+    if (lane == 0 && ntail) atomicAdd(&s.cnt[NB - 1], (uint32_t)ntail);
+    ninf = block_sum_int(ninf, m);
+    if (threadIdx.x == 0) { m->ninf = ninf; m->neg_quota = 0; }
+    __syncthreads();
+    cl.sync();
+
+    if (rank == 0) {
+        for (int b = threadIdx.x; b < NB; b += NT) {
+            uint32_t c = 0;
+            float t = 0.0f;
+            for (int q = 0; q < CL; ++q) {
+                c += peer(cl, s.cnt, q)[b];
+                t += peer(cl, s.tsum, q)[b];
+            }
+            s.cnt[b] = c;
+            s.tsum[b] = t;
+        }
+        __syncthreads();
+        {
+            int part = 0;
+            for (int b = threadIdx.x; b < NB; b += NT) part += (int)s.cnt[b];
+            part = block_sum_int(part, m);
+            if (threadIdx.x == 0) n_finite = part;
+        }
+        // first predictions, from the approximate sums
+        double S_est;
+        block_bin_prefix<double>([&](int b) { return b < NB - 1 ? (double)s.tsum[b] : 0.0; }, s.pref, m, &S_est);
+        uint32_t* cpre = (uint32_t*)s.sstart;  // prefix counts (scratch until the S walk)
+        block_bin_prefix<uint32_t>([&](int b) { return s.cnt[b]; }, cpre, m, (uint32_t*)nullptr);
+        const double u = row_u(a, r.row, p);
+        const double pp = pa ? (double)p.top_p : 1.0;
+        const double D = 2e-3;
+        const long long topn = (a.top_ids && a.top_cap > 0) ? a.top_cap : 0;
+        for (int b = threadIdx.x; b < NB; b += NT) {
+            uint8_t f = 0;
+            int8_t g = 0;
+            if (b < NB - 1 && s.cnt[b] > 0) {
+                const double Pa = s.pref[b], Pb = s.pref[b] + (double)s.tsum[b];
+                bool want = (b == 0) || !(Pa > 0.0);
+                if (!want) {
+                    g = (int8_t)binade_d(Pa);
+                    want = binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
+                }
+                const double ca = Pa / S_est, cb = Pb / S_est;
+                if (pa) {
+                    if (cb >= pp - D && ca <= pp + D) want = true;
+                    if (ca > 0 && ca <= pp + D && binade_d(ca * (1 - D)) != binade_d(cb * (1 + D))) want = true;
+                }
+                const double tgt = u * pp;
+                if (cb >= tgt - D && ca <= tgt + D) want = true;
+                if ((long long)cpre[b] < topn) want = true;
+                f = want ? F_WANT : F_PLAINS;
+            }
+            s.flag[b] = f;
+            s.gs[b] = g;
+            s.gc[b] = 0;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            m->round = 0;
+            m->first_round = 1;
+            m->kmode = 1;
+            m->kfrom = 0;
+            m->kto = NB - 2;
+            m->S_n = 0.0f;
+            w.stage = ST_SWALK;
+            w.swb = 0;
+            w.S = 0.0f;
+            w.cwb = 0;
+            w.C = 0.0f;
+            w.cut_all = 0;
+            w.need = -1;
+        }
+        __syncthreads();
+        bool ovf = false;
+        build_gather_set(s, -1, ovf);
+        push_flags(cl, s);
+    }
+    cl.sync();
+
+    // command loop: every CTA runs CTA 0's pass; CTA 0 then walks
+    while (true) {
+        if (m->cmd == CMD_DONE) break;
+        {
+            const bool first = m->first_round != 0;
+            const int kmode = m->kmode, kfrom = m->kfrom, kto = m->kto;
+            const float Sn = m->S_n;
+            const uint8_t kbit = kmode == 1 ? F_PLAINS : F_PLAINC;
+            for (int b = threadIdx.x; b < NB; b += NT) {
+                if (kmode && b >= kfrom && b <= kto) s.ksum[b] = 0ull;
+                if (first) s.tx[b] = 0ull;
+            }
+            for (int q = threadIdx.x; q < NB / 32; q += NT) s.tie[q] = 0u;
+            __syncthreads();
+            unsigned long long tail_tx = 0ull;
+            const int iters = (r.len + NT - 1) / NT;
+            for (int it = 0; it < iters; ++it) {
+                const int i = it * NT + threadIdx.x;
+                bool want = false;
+                unsigned long long comp = 0;
+                if (i < r.len) {
+                    const float v = s.vals[i];
+                    if (v != NEG_INF) {
+                        const float x = __fsub_rn(v, M);
+                        const int b = binof(x);
+                        const uint8_t f = s.flag[b];
+                        if (f & F_GATH) { want = true; comp = composite(v, r.lo + i); }
+                        if (b < NB - 1) {
+                            const bool needk = kmode && b >= kfrom && b <= kto && (f & kbit);
+                            if (first || needk) {
+                                const float t = qs_expf(x);
+                                if (first) atomicAdd(&s.tx[b], fixed40(t));
+                                if (needk) {
+                                    const float y = kmode == 1 ? __fmul_rn(t, pow2f(23 - s.gs[b]))
+                                                               : __fmul_rn(__fdiv_rn(t, Sn), pow2f(23 - s.gc[b]));
+                                    if ((y - floorf(y)) == 0.5f) atomicOr(&s.tie[b >> 5], 1u << (b & 31));
+                                    atomicAdd(&s.ksum[b], (unsigned long long)rintf(y));
+                                }
+                            }
+                        } else if (first) {
+                            tail_tx += fixed40(__expf(x));
+                        }
+                    }
+                }
+                append_to_leader(cl, s, want, comp);
+            }
+            if (first) {
+                for (int o = 16; o > 0; o >>= 1) tail_tx += __shfl_down_sync(FULLMASK, tail_tx, o);
+                if (lane == 0 && tail_tx) atomicAdd(&s.tx[NB - 1], tail_tx);
+            }
+            // the first neg_quota masked ids of the row (they follow every
+            // finite logit in the sorted order, by ascending id)
+            if (m->neg_quota > 0) {
+                int before = 0;
+                for (int q = 0; q < rank; ++q) before += peer(cl, &m->ninf, q)[0];
+                int quota = m->neg_quota - before;
+                quota = quota < 0 ? 0 : (quota > m->ninf ? m->ninf : quota);
+                int taken = 0;
+                for (int base = 0; base < r.len && taken < quota; base += NT) {
+                    const int i = base + threadIdx.x;
+                    const bool isq = i < r.len && s.vals[i] == NEG_INF;
+                    int tot = 0;
+                    const int rk = block_excl_scan_int(isq ? 1 : 0, tot, m);
+                    append_to_leader(cl, s, isq && taken + rk < quota, composite(NEG_INF, r.lo + i));
+                    taken += tot;
+                }
+            }
+        }
+        __syncthreads();
+        cl.sync();
+        if (rank == 0) {
+            const int kmode = m->kmode, kfrom = m->kfrom, kto = m->kto;
+            const bool first = m->first_round != 0;
+            for (int b = threadIdx.x; b < NB; b += NT) {
+                if (kmode && b >= kfrom && b <= kto) {
+                    unsigned long long k = s.ksum[b];
+                    for (int q = 1; q < CL; ++q) k += peer(cl, s.ksum, q)[b];
+                    s.ksum[b] = k;
+                }
+                if (first) {
+                    unsigned long long t = s.tx[b];
+                    for (int q = 1; q < CL; ++q) t += peer(cl, s.tx, q)[b];
+                    s.tx[b] = t;
+                }
+            }
+            for (int q2 = threadIdx.x; q2 < NB / 32; q2 += NT) {
+                uint32_t t = s.tie[q2];
+                for (int q = 1; q < CL; ++q) t |= peer(cl, s.tie, q)[q2];
+                s.tie[q2] = t;
+            }
+            {
+                const int n = m->spec_n < SPEC_CAP ? m->spec_n : SPEC_CAP;
+                const int P2 = next_pow2(n > 1 ? n : 1);
+                for (int i = n + threadIdx.x; i < P2; i += NT) s.spec[i] = 0ull;
+                __syncthreads();
+                bitonic_desc(s.spec, P2);
+                for (int i = threadIdx.x; i < n; i += NT) s.spect[i] = qs_expf(__fsub_rn(comp_val(s.spec[i]), M));
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                m->first_round = 0;
+                m->kmode = 0;
+                m->cmd = CMD_DONE;
+                w.need = -1;
+            }
+            __syncthreads();
+
+            // ---- walk state machine: runs until it needs a pass or is done
+            bool go = true;
+            while (go) {
+                go = false;
+                const int stage = w.stage;
+                if (stage == ST_SWALK) {
+                    if (threadIdx.x < 32) {
+                        float S = w.S;
+                        int b = w.swb;
+                        while (true) {
+                            b = warp_walk_bins(S, b, NB - 1, s, s.gs, F_PLAINS, POS_INF, true);
+                            if (b >= NB - 1 || !(s.flag[b] & F_GATH)) break;
+                            const uint32_t off = s.specoff[b];
+                            if (threadIdx.x == 0) s.sstart[b] = S;
+                            warp_walk_terms(S, (int)s.cnt[b], POS_INF, [&](int i) { return s.spect[off + i]; });
+                            ++b;
+                        }
+                        if (threadIdx.x == 0) {
+                            w.S = S;
+                            w.swb = b;
+                            if (b >= NB - 1) {
+                                m->S_n = S;
+                                if (pa) {
+                                    w.stage = ST_CUMPREP;
+                                } else {
+                                    w.stage = ST_DRAW;
+                                    w.cut_all = 1;
+                                    w.n_keep = NSEL;
+                                    w.Sc = S;
+                                    w.mass_cut = 0.0;
+                                }
+                            } else {
+                                w.need = b;
+                            }
+                        }
+                    }
+                    __syncthreads();
+                    if (w.need >= 0) {
+                        // re-predict the rest from the exact running sum
+                        const int fb = w.need;
+                        __syncthreads();
+                        block_bin_prefix<double>([&](int b) { return b < NB - 1 ? (double)s.tx[b] * 0x1p-40 : 0.0; },
+                                                 s.pref, m, (double*)nullptr);
+                        const double P = s.pref[fb];
+                        const double ratio = P > 0.0 ? (double)w.S / P : 1.0;
+                        __syncthreads();
+                        predict_s(s, fb, ratio);
+                    } else {
+                        go = true;
+                    }
+                } else if (stage == ST_CUMPREP) {
+                    predict_c(s, 0, 1.0, p.top_p);
+                    if (threadIdx.x == 0) {
+                        w.stage = ST_CUMWALK;
+                        w.need = 0;  // a pass (bin 0 is gathered again)
+                    }
+                    __syncthreads();
+                } else if (stage == ST_CUMWALK) {
+                    const float Sn = m->S_n;
+                    if (threadIdx.x < 32) {
+                        float C = w.C;
+                        int b = w.cwb;
+                        int found = -1;
+                        while (true) {
+                            b = warp_walk_bins(C, b, NB - 1, s, s.gc, F_PLAINC, p.top_p, false);
+                            if (b >= NB - 1 || !(s.flag[b] & F_GATH)) break;
+                            const uint32_t off = s.specoff[b];
+                            const int n = (int)s.cnt[b];
+                            const int idx = warp_walk_terms(C, n, p.top_p, [&](int i) { return __fdiv_rn(s.spect[off + i], Sn); });
+                            if (idx < n) { found = idx; break; }
+                            ++b;
+                        }
+                        if (found >= 0) {
+                            // S at the cutoff: the S walk's state at the bin start plus the bin's prefix
+                            float S = s.sstart[b];
+                            const uint32_t off = s.specoff[b];
+                            warp_walk_terms(S, found + 1, POS_INF, [&](int i) { return s.spect[off + i]; });
+                            if (threadIdx.x == 0) {
+                                double mc = 0.0;
+                                for (int i = 0; i <= found; ++i) mc += (double)__fdiv_rn(s.spect[off + i], S);
+                                w.cut_bin = b;
+                                w.cut_idx = found;
+                                w.Sc = S;
+                                w.mass_cut = mc;
+                            }
+                        }
+                        if (threadIdx.x == 0) {
+                            w.C = C;
+                            w.cwb = b;
+                            if (found >= 0) {
+                                w.cut_all = 0;
+                                w.stage = ST_DRAW;
+                            } else if (b >= NB - 1) {
+                                w.cut_all = 1;
+                                w.n_keep = NSEL;
+                                w.Sc = Sn;
+                                w.mass_cut = 0.0;
+                                w.stage = ST_DRAW;
+                            } else {
+                                w.need = b;
+                            }
+                        }
+                    }
+                    __syncthreads();
+                    if (w.need >= 0) {
+                        const int fb = w.need;
+                        block_bin_prefix<double>([&](int b) { return b < NB - 1 ? (double)s.tx[b] * 0x1p-40 : 0.0; },
+                                                 s.pref, m, (double*)nullptr);
+                        const double P = s.pref[fb] / (double)Sn;
+                        const double ratio = P > 0.0 ? (double)w.C / P : 1.0;
+                        __syncthreads();
+                        predict_c(s, fb, ratio, p.top_p);
+                    } else {
+                        if (w.stage == ST_DRAW && !w.cut_all) {
+                            int part = 0;
+                            for (int b = threadIdx.x; b < w.cut_bin; b += NT) part += (int)s.cnt[b];
+                            part = block_sum_int(part, m);
+                            if (threadIdx.x == 0) w.n_keep = (long long)part + w.cut_idx + 1;
+                            __syncthreads();
+                        }
+                        go = true;
+                    }
+                } else if (stage == ST_DRAW) {
+                    // Survivors: ranks [0, n_keep), probabilities p_i = t_i / Sc.
+                    // Whole bins below the cutoff bin count by their t sums,
+                    // the cutoff bin by its survivors (mass_cut).
+                    const int bc = w.cut_all ? NB : w.cut_bin;
+                    const double Sc = (double)w.Sc;
+                    const long long c = w.n_keep;
+                    double* mpre = s.pref;
+                    double dsum = 0.0;
+                    block_bin_prefix<double>([&](int b) {
+                        return b < bc ? (double)s.tx[b] * 0x1p-40 / Sc : (b == bc ? w.mass_cut : 0.0);
+                    }, mpre, m, &dsum);
+                    uint32_t* cpre = (uint32_t*)s.sstart;  // the S walk's starts are no longer needed
+                    block_bin_prefix<uint32_t>([&](int b) { return s.cnt[b]; }, cpre, m, (uint32_t*)nullptr);
+                    __shared__ int d_bin;
+                    __shared__ double d_tgt;
+                    if (threadIdx.x == 0) { d_bin = 0x7fffffff; d_tgt = c >= 2 ? row_u(a, r.row, p) * dsum : 0.0; }
+                    for (int b = threadIdx.x; b < NB; b += NT) s.flag[b] &= (uint8_t)~F_WANT;
+                    __syncthreads();
+                    const double tgt = d_tgt;
+                    for (int b = threadIdx.x; b < NB && b <= bc; b += NT) {
+                        const double mb = b < bc ? (double)s.tx[b] * 0x1p-40 / Sc : w.mass_cut;
+                        if (s.cnt[b] > 0 && (c < 2 || mpre[b] + mb >= tgt)) atomicMin(&d_bin, b);
+                    }
+                    __syncthreads();
+                    if (threadIdx.x == 0) {
+                        int dbin = d_bin;
+                        if (dbin == 0x7fffffff) {  // target past the total (u ~ 1): the last survivor
+                            dbin = (bc < NB ? bc : NB - 1);
+                            while (dbin > 0 && s.cnt[dbin] == 0) --dbin;
+                        }
+                        w.dbin = dbin;
+                        w.acc = mpre[dbin];
+                        w.tgt = tgt;
+                        w.draw_rank = cpre[dbin];
+                        const bool in_cut = !w.cut_all && dbin == bc;
+                        w.big = (!in_cut && c >= 2 && (int)s.cnt[dbin] > SPEC_CAP / 2) ? 1 : 0;
+                        int need = -1;
+                        if (!w.big) {
+                            s.flag[dbin] |= F_WANT;
+                            if (!(s.flag[dbin] & F_GATH)) need = dbin;
+                        }
+                        if (a.top_ids && a.top_cap > 0) {
+                            long long accn = 0;
+                            const long long lim = c < a.top_cap ? c : a.top_cap;
+                            for (int b = 0; b < NB && accn < lim; ++b) {
+                                if (!s.cnt[b]) continue;
+                                s.flag[b] |= F_WANT;
+                                if (!(s.flag[b] & F_GATH) && need < 0) need = b;
+                                accn += s.cnt[b];
+                            }
+                            const int negq = lim > n_finite ? (int)(lim - n_finite) : 0;
+                            if (negq > m->neg_quota || (negq > 0 && need >= 0)) {
+                                m->neg_quota = negq;
+                                if (need < 0) need = dbin;
+                            }
+                        }
+                        w.need = need;
+                    }
+                    __syncthreads();
+                    if (w.need < 0) {
+                        if (w.big) {
+                            int id;
+                            long long before;
+                            float pr;
+                            leader_weighted_select(cl, s, a.n_s, r.V, w.dbin, (w.tgt - w.acc) * (double)w.Sc, M, w.Sc,
+                                                   id, before, pr);
+                            if (threadIdx.x == 0) {
+                                w.draw_id = id;
+                                w.draw_rank += before;
+                                w.draw_prob = pr;
+                            }
+                        } else if (threadIdx.x == 0) {
+                            const int dbin = w.dbin;
+                            const uint32_t off = s.specoff[dbin];
+                            int n = (int)s.cnt[dbin];
+                            if (!w.cut_all && dbin == bc) n = w.cut_idx + 1;
+                            int jj = n - 1;
+                            double acc = w.acc;
+                            if (c >= 2) {
+                                for (int i = 0; i < n; ++i) {
+                                    acc += (double)__fdiv_rn(s.spect[off + i], w.Sc);
+                                    if (acc >= w.tgt) { jj = i; break; }
+                                }
+                            } else {
+                                jj = 0;
+                            }
+                            w.draw_id = comp_idx(s.spec[off + jj]);
+                            w.draw_prob = __fdiv_rn(s.spect[off + jj], w.Sc);
+                            w.draw_rank += jj;
+                        }
+                        if (threadIdx.x == 0) {
+                            w.drew = c >= 2 ? 1 : 0;
+                            w.stage = ST_FINISH;
+                        }
+                        __syncthreads();
+                        go = true;
+                    } else {
+                        // the pass gathers what the draw and the survivor list need
+                        if (threadIdx.x == 0) m->kmode = 0;
+                        __syncthreads();
+                    }
+                } else if (stage == ST_FINISH) {
+                    if (threadIdx.x == 0) {
+                        qsamp_row_result res;
+                        res.token = w.draw_id;
+                        res.position = (int)w.draw_rank;
+                        res.n_keep = (int)w.n_keep;
+                        res.drew = w.drew;
+                        res.sum_exp = pa ? m->S_n : 0.0f;
+                        res.sum_keep = w.Sc;
+                        res.max_logit = M;
+                        res.prob = w.draw_prob;
+                        write_result(a, r.row, res);
+                        m->cmd = CMD_DONE;
+                    }
+                    if (a.top_ids) {
+                        // the first ranks: gathered bins from bin 0 on are contiguous in the list
+                        const long long c = w.n_keep;
+                        for (int i = threadIdx.x; i < a.top_cap; i += NT) {
+                            const bool in = i < c && i < SPEC_CAP;
+                            a.top_ids[(size_t)r.row * a.top_cap + i] = in ? comp_idx(s.spec[i]) : -1;
+                            a.top_probs[(size_t)r.row * a.top_cap + i] = in ? __fdiv_rn(s.spect[i], w.Sc) : 0.0f;
+                        }
+                    }
+                    __syncthreads();
+                }
+            }
+            if (w.need >= 0) {
+                bool ovf = false;
+                if (m->round >= a.max_rounds) ovf = true;
+                else build_gather_set(s, w.need, ovf);
+                if (ovf) {
+                    if (threadIdx.x == 0) {
+                        set_status(a.status, DEV_ROUNDS_EXHAUSTED);
+                        // diagnostics: stage, bin, its size, rounds used
+                        qsamp_row_result res = {};
+                        res.token = -1;
+                        res.position = w.stage;
+                        res.n_keep = w.need;
+                        res.drew = (int)s.cnt[w.need];
+                        res.prob = (float)m->round;
+                        write_result(a, r.row, res);
+                        m->cmd = CMD_DONE;
+                    }
+                    __syncthreads();
+                }
+            }
+            push_flags(cl, s);
+        }
+        cl.sync();
+    }
+}
+
+// ------------------------------------------------------------ the kernel
+__global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
+    cg::cluster_group cl = cg::this_cluster();
+    const int rank = (int)cl.block_rank();
+    const int CL = (int)cl.num_blocks();
+    const int cid = blockIdx.x / CL;
+    const int ncl = gridDim.x / CL;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const Sm s = carve(smem_raw, a.n_s);
+    Misc* m = s.misc;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+
+    for (int row = cid; row < a.B; row += ncl) {
+        if (threadIdx.x == 0) m->prm = a.params[row];
+        __syncthreads();
+        const qsamp_row_params& p = m->prm;
+        RowCtx r;
+        r.p = &m->prm;
+        r.row = row;
+        r.V = a.V;
+        r.lo = rank * a.n_s;
+        r.hi = min(a.V, r.lo + a.n_s);
+        r.len = r.hi > r.lo ? r.hi - r.lo : 0;
+        const size_t esz = a.dtype == QSAMP_BF16 ? 2 : 4;
+        r.rowp = (const char*)a.logits + (size_t)row * (size_t)a.row_stride * esz;
+        r.dtype = a.dtype;
+        r.cap = p.softcap;
+        r.cap_on = p.softcap > 0.0f;
+        r.T = p.temperature;
+        r.div_on = p.temperature > 0.0f && p.temperature != 1.0f;
+        r.force = p.force_token;
+        r.force_on = p.force_token >= 0 && p.force_token < a.V;
+        r.mask = a.masks ? a.masks + (size_t)row * (size_t)a.mask_stride : nullptr;
+        r.lut = nullptr;
+        if (r.cap_on && a.dtype == QSAMP_BF16 && a.luts) {
+            for (int q = 0; q < MAX_LUT; ++q)
+                if (a.lut_caps[q] == p.softcap) r.lut = a.luts + (size_t)q * 65536;
+        }
+
+        transform_slice(r, a, s);
+        __syncthreads();
+        penalty_fixup(r, a, s);
+
+        // row max (lowest id among equal maxima, as std::max_element)
+        float bm = NEG_INF;
+        int bi = 0x7fffffff;
+        for (int i = threadIdx.x; i < r.len; i += NT) {
+            const float v = s.vals[i];
+            if (v > bm || (v == bm && r.lo + i < bi)) { bm = v; bi = r.lo + i; }
+        }
+        int bidx;
+        bm = block_reduce_max_idx(bm, bi, bidx, m);
+        if (threadIdx.x == 0) { m->cmax = bm; m->cmax_idx = bidx; }
+        __syncthreads();
+        cl.sync();
+        if (threadIdx.x == 0) {
+            float gm = NEG_INF;
+            int gi = 0x7fffffff;
+            for (int q = 0; q < CL; ++q) {
+                const Misc* pm = peer(cl, m, q);
+                const float v = pm->cmax;
+                const int i = pm->cmax_idx;
+                if (v > gm || (v == gm && i < gi)) { gm = v; gi = i; }
+            }
+            m->M = gm;
+            m->argmax = gi == 0x7fffffff ? 0 : gi;
+        }
+        __syncthreads();
+
+        const float M = m->M;
+        const int V = a.V;
+        const int n = (p.top_k > 0 && p.top_k < V) ? p.top_k : V;
+        if (p.temperature <= 0.0f) {
+            if (rank == 0 && threadIdx.x == 0) {
+                qsamp_row_result res;
+                res.token = m->argmax;
+                res.position = 0;
+                res.n_keep = 1;
+                res.drew = 0;
+                res.sum_exp = 0.0f;
+                res.sum_keep = 0.0f;
+                res.max_logit = M;
+                res.prob = 1.0f;
+                write_result(a, row, res);
+            }
+            if (rank == 0 && a.top_ids)
+                for (int i = threadIdx.x; i < a.top_cap; i += NT) {
+                    a.top_ids[(size_t)row * a.top_cap + i] = i == 0 ? m->argmax : -1;
+                    a.top_probs[(size_t)row * a.top_cap + i] = i == 0 ? 1.0f : 0.0f;
+                }
+        } else if (M == NEG_INF) {
+            // every logit masked: the reference's weights are NaN; report the
+            // first sorted id (id 0) without drawing.
+            if (rank == 0 && threadIdx.x == 0) {
+                qsamp_row_result res = {};
+                res.token = 0;
+                res.n_keep = n;
+                res.max_logit = M;
+                res.prob = __int_as_float(0x7fc00000);
+                write_result(a, row, res);
+            }
+            if (rank == 0 && a.top_ids)
+                for (int i = threadIdx.x; i < a.top_cap; i += NT) {
+                    a.top_ids[(size_t)row * a.top_cap + i] = -1;
+                    a.top_probs[(size_t)row * a.top_cap + i] = 0.0f;
+                }
+        } else if (n < V && n <= KMAX) {
+            topk_path(cl, r, a, s, n);
+        } else {
+            if (n < V) restrict_to_topk(cl, r, s, n);
+            if (threadIdx.x == 0) m->n_sel = n;
+            __syncthreads();
+            full_path(cl, r, a, s);
+        }
+        __syncthreads();
+        cl.sync();
+    }
+}
+
+// Soft-cap table for bf16 inputs: lut[b] = cap * tanh(bf16(b) / cap).
+__global__ void qs_softcap_lut_kernel(float* lut, float cap) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < 65536) lut[i] = qs_softcap(qs_bf16_to_f32((uint16_t)i), cap);
+}
+
+}  // namespace qs
+
+// launch helpers used by qsamp_api.cu
+extern "C" cudaError_t qs_launch_rows(const qs::QsLaunch* a, int clusters, int cl, size_t smem, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(clusters * cl));
+    cfg.blockDim = dim3(qs::NT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, qs::qs_rows_kernel, *a);
+}
+
+extern "C" cudaError_t qs_kernel_static_smem(size_t* out) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, qs::qs_rows_kernel);
+    if (e == cudaSuccess) *out = fa.sharedSizeBytes;
+    return e;
+}
+
+extern "C" cudaError_t qs_kernel_attrs(size_t smem) {
+    cudaError_t e = cudaFuncSetAttribute(qs::qs_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(qs::qs_rows_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+
+extern "C" cudaError_t qs_max_clusters(int cl, size_t smem, int* out) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(cl * 64));
+    cfg.blockDim = dim3(qs::NT);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaOccupancyMaxActiveClusters(out, (void*)qs::qs_rows_kernel, &cfg);
+}
+
+extern "C" cudaError_t qs_launch_lut(float* lut, float cap, cudaStream_t st) {
+    qs::qs_softcap_lut_kernel<<<65536 / 256, 256, 0, st>>>(lut, cap);
+    return cudaGetLastError();
+}

@@ -1,0 +1,161 @@
+"""GPU parity: the CUDA path (through the C ABI) against the C restatement.
+
+Both evaluate the reference's stage order with IEEE float in source order and
+order equal logits by ascending id, so every field of every row must match
+bit for bit: token, rank, survivors, whether u was consumed, the top-p and
+softmax denominators, the max logit and the token's probability.
+"""
+import numpy as np
+import pytest
+
+from qwenium_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+FIELDS = ("token", "position", "n_keep", "drew", "sum_exp", "sum_keep", "max_logit", "prob")
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from qwenium_b200 import qsamp
+
+    return qsamp.Context(0)
+
+
+def run_gpu(ctx, cfg, top_cap=0, host=False):
+    import torch
+
+    x = cfg["logits"]
+    B, V = x.shape
+    if host:
+        ids, res, ti, tp = ctx.sample_host(x, cfg["params"], cfg.get("hist"), cfg.get("hist_len"), cfg.get("masks"),
+                                           cfg["u"], top_cap=top_cap, bf16=cfg["bf16"])
+        return res, ti, tp
+    if cfg["bf16"]:
+        dx = torch.from_numpy(x.view(np.int16)).cuda()
+    else:
+        dx = torch.from_numpy(x).cuda()
+    hist = torch.from_numpy(cfg["hist"]).cuda() if cfg.get("hist") is not None else None
+    masks = torch.from_numpy(cfg["masks"].view(np.int32)).cuda() if cfg.get("masks") is not None else None
+    ids = torch.empty(B, dtype=torch.int32, device="cuda")
+    ti = torch.empty((B, max(top_cap, 1)), dtype=torch.int32, device="cuda") if top_cap else None
+    tp = torch.empty((B, max(top_cap, 1)), dtype=torch.float32, device="cuda") if top_cap else None
+    res = ctx.sample_batch(dx, cfg["params"], hist=hist, hist_len=cfg.get("hist_len"), masks=masks, u=cfg["u"],
+                           out_ids=ids, top_cap=top_cap, out_top_ids=ti, out_top_probs=tp)
+    torch.cuda.synchronize()
+    r = res.cpu().numpy().view(np.dtype([(f, "<i4" if f in FIELDS[:4] else "<f4") for f in FIELDS])).reshape(B)
+    assert np.array_equal(ids.cpu().numpy(), r["token"])
+    return r, (ti.cpu().numpy() if ti is not None else None), (tp.cpu().numpy() if tp is not None else None)
+
+
+def run_oracle(O, cfg, top_cap=0):
+    out, ti, tp, _ = O.oracle_sample(cfg["logits"], cfg["params"], cfg.get("hist"), cfg.get("hist_len"),
+                                     cfg.get("masks"), cfg["u"], top_cap=top_cap, bf16=cfg["bf16"])
+    return out, ti, tp
+
+
+def assert_same(gpu, ora, label=""):
+    g, gti, gtp = gpu
+    o, oti, otp = ora
+    bad = []
+    for b in range(len(o)):
+        for f in FIELDS:
+            gv, ov = g[b][f], o[b][f]
+            if f in FIELDS[:4]:
+                same = int(gv) == int(ov)
+            else:
+                same = np.float32(gv).view(np.uint32) == np.float32(ov).view(np.uint32) or (np.isnan(gv) and np.isnan(ov))
+            if not same:
+                bad.append((b, f, gv, ov))
+    if gti is not None and oti is not None:
+        for b in range(len(o)):
+            if not np.array_equal(gti[b], oti[b]):
+                bad.append((b, "top_ids", gti[b][:8], oti[b][:8]))
+            if not np.array_equal(gtp[b].view(np.uint32), otp[b].view(np.uint32)):
+                bad.append((b, "top_probs", gtp[b][:4], otp[b][:4]))
+    assert not bad, f"{label}: {len(bad)} mismatches, first: {bad[:6]}"
+
+
+def check(ctx, O, cfg, top_cap=16, host=False):
+    assert_same(run_gpu(ctx, cfg, top_cap, host), run_oracle(O, cfg, top_cap), cfg["name"])
+
+
+def test_config1(ctx, oracle_mod):
+    check(ctx, oracle_mod, W.config1(1))
+    check(ctx, oracle_mod, W.config1(3))
+
+
+def test_config1_greedy(ctx, oracle_mod):
+    check(ctx, oracle_mod, W.config1(1, greedy=True))
+
+
+def test_config2(ctx, oracle_mod):
+    check(ctx, oracle_mod, W.config2(2, B=10))
+
+
+def test_config2_more_rows(ctx, oracle_mod):
+    check(ctx, oracle_mod, W.config2(21, B=64))
+
+
+def test_config4_subset(ctx, oracle_mod):
+    check(ctx, oracle_mod, W.config4(4, B=16))
+
+
+def test_config5_subset(ctx, oracle_mod):
+    check(ctx, oracle_mod, W.config5(5, B=16))
+
+
+def test_host_entry_point(ctx, oracle_mod):
+    check(ctx, oracle_mod, W.config2(22, B=6), host=True)
+
+
+def _edge_cfg(seed, V, B=12):
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((B, V)) * rng.uniform(0.5, 6)).astype(np.float32)
+    if rng.random() < 0.5:  # tie-heavy rows
+        x = W.bf16_bits_to_f32(W.f32_to_bf16_bits(x))
+    p = W.default_params(B)
+    p["temperature"] = rng.choice([0.0, 0.3, 0.8, 1.0, 1.7], B)
+    p["top_k"] = rng.choice([0, 1, 5, max(V - 1, 0), V, V + 3], B)
+    p["top_p"] = rng.choice([0.0, 0.5, 0.9, 0.95, 1.0], B)
+    p["repetition_penalty"] = rng.choice([1.0, 1.1, 1.3], B)
+    p["repetition_lookback"] = rng.choice([0, 16, 64, -1], B)
+    p["frequency_penalty"] = rng.choice([0.0, 0.2], B)
+    p["presence_penalty"] = rng.choice([0.0, 0.3], B)
+    p["softcap"] = rng.choice([0.0, 0.0, 5.0], B)
+    H = 48
+    hist = rng.integers(-2, V + 2, size=(B, H), dtype=np.int64).astype(np.int32)
+    hl = rng.integers(0, H + 1, size=B).astype(np.int32)
+    words = (V + 31) // 32
+    masks = None
+    if rng.random() < 0.6:
+        keep = rng.random((B, V)) < rng.uniform(0.05, 1.0)
+        keep[:, 0] |= ~keep.any(axis=1)
+        masks = np.zeros((B, words), np.uint32)
+        for b in range(B):
+            ids = np.nonzero(keep[b])[0]
+            np.bitwise_or.at(masks[b], ids >> 5, (np.uint32(1) << (ids & 31).astype(np.uint32)))
+    for b in range(B):
+        if rng.random() < 0.1:
+            p["force_token"][b] = rng.integers(0, V)
+    seeds = rng.integers(0, 2**32, size=B, dtype=np.uint64).astype(np.uint32)
+    return dict(name=f"edge-V{V}-s{seed}", logits=x, bf16=False, params=p, hist=hist, hist_len=hl, masks=masks,
+                seeds=seeds, u=W.uniforms_for(seeds))
+
+
+@pytest.mark.parametrize("V", [1, 2, 3, 31, 32, 33, 257, 4097, 40000])
+def test_edge_vocab_sizes(ctx, oracle_mod, V):
+    for seed in range(3):
+        check(ctx, oracle_mod, _edge_cfg(1000 * V + seed, V))
+
+
+def test_all_masked_and_forced(ctx, oracle_mod):
+    cfg = _edge_cfg(5, 1000, B=4)
+    cfg["masks"] = np.zeros((4, 32), np.uint32)
+    cfg["params"]["force_token"] = [-1, 7, -1, 999]
+    cfg["params"]["temperature"] = [0.0, 0.8, 1.0, 0.0]
+    check(ctx, oracle_mod, cfg)
