@@ -110,6 +110,27 @@ qsamp_status qsamp_sample(qsamp_ctx* ctx, const qsamp_batch* batch, void* stream
  * logits live on the host. */
 qsamp_status qsamp_sample_host(qsamp_ctx* ctx, const qsamp_batch* batch);
 
+/* Allocation-free selection. No counterpart in the reference: it exists
+ * for callers that may not allocate device memory when they sample (a
+ * serving engine that reserves all device memory up front, a plugin host
+ * that forbids cudaMalloc, code running under someone else's graph-capture
+ * rules). qsamp_create allocates, so this entry point takes no context.
+ *
+ * Same batch semantics as qsamp_sample (logits, hist, masks and outputs in
+ * device memory; params, hist_len and u on the host). Its scratch is one
+ * static device array of QSAMP_STATIC_SCRATCH_BYTES that every GPU loading
+ * the library holds until the process exits; it serves at most
+ * QSAMP_STATIC_MAX_ROWS rows per call (more: QSAMP_ERR_INVALID_ARG) and one
+ * bf16 soft-cap table per call (rows with a second cap value compute tanh per
+ * logit). The first call on a device, with that device current, looks up the
+ * array's device address; make it before any stream capture. All calls on a
+ * device share the array, so calls whose work overlaps on the GPU race.
+ * Device-side limits are reported in the row results (token -1). err, when
+ * non-NULL, receives a message of at most err_len bytes. */
+#define QSAMP_STATIC_MAX_ROWS 4096
+#define QSAMP_STATIC_SCRATCH_BYTES (640u * 1024u)
+qsamp_status qsamp_sample_static(const qsamp_batch* batch, void* stream, char* err, size_t err_len);
+
 /* Host helpers for the allow-mask. -------------------------------------- */
 
 /* Pack ids into allow-bits (words = ceil(V/32), zeroed first); ids outside

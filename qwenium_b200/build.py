@@ -9,7 +9,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libqsamp.so")
-SOURCES = [os.path.join(CSRC, f) for f in ("qsamp_kernels.cu", "qsamp_api.cu")]
+SOURCES = [os.path.join(CSRC, f) for f in ("qsamp_kernels.cu", "qsamp_api.cu", "qsamp_static.cu")]
 HEADERS = [os.path.join(CSRC, f) for f in ("qs_math.h", "qsamp_device.h")] + [os.path.join(ROOT, "include", "qsamp.h")]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # IEEE float semantics are part of the contract: no --use_fast_math.

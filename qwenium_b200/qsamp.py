@@ -62,7 +62,7 @@ STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "UNSUPPORTED", 4: "DEVICE", 5
 EXPORTS = (
     "qsamp_create", "qsamp_destroy", "qsamp_last_error", "qsamp_sample", "qsamp_sample_host",
     "qsamp_pack_ids", "qsamp_grammar_mask", "qsamp_find_eos_string", "qsamp_keep_list_mask",
-    "qsamp_mask_and", "qsamp_shard_topk", "qsamp_merge_topk", "qsamp_get_counters",
+    "qsamp_mask_and", "qsamp_shard_topk", "qsamp_merge_topk", "qsamp_get_counters", "qsamp_sample_static",
 )
 
 _P = ctypes.c_void_p
@@ -147,6 +147,8 @@ def load(path: str = LIB_PATH):
                                      ctypes.c_uint64, _P, _P, _P]
     lib.qsamp_get_counters.restype = ctypes.c_int
     lib.qsamp_get_counters.argtypes = [_P, ctypes.POINTER(_Counters)]
+    lib.qsamp_sample_static.restype = ctypes.c_int
+    lib.qsamp_sample_static.argtypes = [ctypes.POINTER(_Batch), _P, ctypes.c_char_p, ctypes.c_size_t]
     _lib = lib
     return lib
 
@@ -439,3 +441,32 @@ class TemperatureSampler(Sampler):
         if self.uniform is None:
             return None
         return np.array([self.uniform()], np.float64)
+
+
+STATIC_MAX_ROWS = 4096  # QSAMP_STATIC_MAX_ROWS in include/qsamp.h
+
+
+def sample_static(logits, params, hist=None, hist_len=None, masks=None, u=None, rng_offset=0, out_ids=None,
+                  out_results=None, stream=None):
+    """qsamp_sample_static: the allocation-free entry point (no context).
+    Same arguments as Context.sample_batch; every output must be supplied."""
+    import torch
+
+    lib = load()
+    B, V = int(logits.shape[0]), int(logits.shape[1])
+    dtype = QSAMP_BF16 if logits.dtype in (torch.bfloat16, torch.int16, torch.uint16) else QSAMP_F32
+    params = np.ascontiguousarray(params, ROW_PARAMS)
+    if hist_len is not None:
+        hist_len = np.ascontiguousarray(hist_len, np.int32)
+    if u is not None:
+        u = np.ascontiguousarray(u, np.float64)
+    if stream is None:
+        stream = torch.cuda.current_stream(logits.device).cuda_stream
+    mstride = int(masks.stride(0)) if masks is not None and masks.dim() == 2 else 0
+    b = Context._batch(logits.data_ptr(), dtype, B, V, int(logits.stride(0)), params, _dev_ptr(hist),
+                       int(hist.stride(0)) if hist is not None else 0, hist_len, _dev_ptr(masks), mstride, u,
+                       rng_offset, _dev_ptr(out_ids), _dev_ptr(out_results), None, None, 0)
+    err = ctypes.create_string_buffer(512)
+    rc = lib.qsamp_sample_static(ctypes.byref(b), ctypes.c_void_p(stream), err, len(err))
+    if rc:
+        raise QsampError(rc, "qsamp_sample_static: " + err.value.decode(errors="replace"))
