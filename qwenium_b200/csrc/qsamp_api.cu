@@ -18,6 +18,10 @@ extern "C" cudaError_t qs_kernel_attrs(size_t smem);
 extern "C" cudaError_t qs_kernel_static_smem(size_t* out);
 extern "C" cudaError_t qs_max_clusters(int cl, size_t smem, int* out);
 extern "C" cudaError_t qs_launch_lut(float* lut, float cap, cudaStream_t st);
+extern "C" size_t qs_stream_smem(int V);
+extern "C" cudaError_t qs_stream_attrs(size_t smem);
+extern "C" cudaError_t qs_stream_occupancy(size_t smem, int* blocks_per_sm);
+extern "C" cudaError_t qs_launch_stream(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st);
 extern "C" cudaError_t qs_launch_shard(const qs::QsLaunch* a, int clusters, int cl, size_t smem, int v_offset,
                                        int k, float* cand_vals, int32_t* cand_ids, cudaStream_t st);
 extern "C" cudaError_t qs_launch_merge(int n_ranks, int B, int k, const float* vals, const int32_t* ids,
@@ -60,6 +64,9 @@ struct qsamp_ctx {
     DevBuf<int32_t> hist_len;
     DevBuf<double> u;
     DevBuf<qsamp_row_result> results;
+    DevBuf<int32_t> rows;          // row lists: streamed rows, then cluster rows
+    std::vector<int32_t> h_rows;
+    size_t stream_attr = 0;
     DevBuf<int> status;
     DevBuf<float> luts;
     float lut_caps[qs::MAX_LUT] = {0, 0, 0, 0};
@@ -325,10 +332,43 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     }
     s = ensure_luts(c, b, st);
     if (s != QSAMP_OK) return s;
-    Plan plan;
-    s = plan_for(c, B, b->V, plan);
-    if (s != QSAMP_OK) return s;
     if ((e = cudaMemsetAsync(c->status.p, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail(c, e, "status reset");
+
+    // Route rows: greedy rows and top-k rows (k <= 1024) with a penalty
+    // window of at most 1024 ids stream through one CTA each; the rest (full
+    // vocabulary, large k, long windows) use the cluster kernel.
+    const size_t sn_smem = qs_stream_smem(b->V);
+    const bool stream_fits = sn_smem <= c->max_dyn || c->max_dyn == 0;
+    c->h_rows.resize((size_t)B);
+    int n_stream = 0, n_cluster = 0;
+    for (int r = 0; r < B; ++r) {
+        const qsamp_row_params& p = b->params[r];
+        bool st_ok = stream_fits && (p.temperature <= 0.0f || (p.top_k > 0 && p.top_k < b->V && p.top_k <= qs::KMAX));
+        if (st_ok && b->hist) {
+            const bool pen = p.repetition_penalty != 1.0f || p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
+            const int len = b->hist_len ? b->hist_len[r] : b->hist_stride;
+            const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
+            const long long w = (long long)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
+            if (pen && w > 1024) st_ok = false;
+        }
+        if (st_ok) c->h_rows[(size_t)n_stream++] = r;
+    }
+    for (int r = 0, j = n_stream; r < B; ++r) {
+        const qsamp_row_params& p = b->params[r];
+        bool st_ok = stream_fits && (p.temperature <= 0.0f || (p.top_k > 0 && p.top_k < b->V && p.top_k <= qs::KMAX));
+        if (st_ok && b->hist) {
+            const bool pen = p.repetition_penalty != 1.0f || p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
+            const int len = b->hist_len ? b->hist_len[r] : b->hist_stride;
+            const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
+            const long long w = (long long)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
+            if (pen && w > 1024) st_ok = false;
+        }
+        if (!st_ok) c->h_rows[(size_t)j++] = r, ++n_cluster;
+    }
+    if ((e = c->rows.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(rows)");
+    if ((e = cudaMemcpyAsync(c->rows.p, c->h_rows.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice, st)) !=
+        cudaSuccess)
+        return cuda_fail(c, e, "copying row lists");
 
     qs::QsLaunch a = {};
     a.logits = b->logits;
@@ -354,10 +394,33 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     a.top_probs = b->top_cap > 0 ? b->out_top_probs : nullptr;
     a.top_cap = b->top_cap;
     a.status = c->status.p;
-    a.n_s = plan.n_s;
     a.max_rounds = kMaxRounds;
-    e = qs_launch_rows(&a, plan.clusters, plan.cl, plan.smem, st);
-    if (e != cudaSuccess) return cuda_fail(c, e, "selection kernel launch");
+    if (n_stream > 0) {
+        if (sn_smem > c->stream_attr) {
+            if ((e = qs_stream_attrs(sn_smem)) != cudaSuccess) return cuda_fail(c, e, "stream kernel attributes");
+            c->stream_attr = sn_smem;
+        }
+        int per_sm = 0;
+        if ((e = qs_stream_occupancy(sn_smem, &per_sm)) != cudaSuccess || per_sm <= 0)
+            return cuda_fail(c, e == cudaSuccess ? cudaErrorInvalidConfiguration : e, "stream kernel occupancy");
+        qs::QsLaunch sa = a;
+        sa.rows = c->rows.p;
+        sa.nrows = n_stream;
+        const int grid = n_stream < per_sm * c->num_sms ? n_stream : per_sm * c->num_sms;
+        if ((e = qs_launch_stream(&sa, grid, sn_smem, st)) != cudaSuccess)
+            return cuda_fail(c, e, "stream kernel launch");
+    }
+    if (n_cluster > 0) {
+        Plan plan;
+        s = plan_for(c, n_cluster, b->V, plan);
+        if (s != QSAMP_OK) return s;
+        qs::QsLaunch ca = a;
+        ca.rows = c->rows.p + n_stream;
+        ca.nrows = n_cluster;
+        ca.n_s = plan.n_s;
+        e = qs_launch_rows(&ca, plan.clusters, plan.cl, plan.smem, st);
+        if (e != cudaSuccess) return cuda_fail(c, e, "selection kernel launch");
+    }
     c->ctr.calls += 1;
     c->ctr.rows += (uint64_t)B;
     c->ctr.logit_bytes += (uint64_t)B * (uint64_t)b->V * esz;

@@ -26,6 +26,7 @@ enum DevStatus : int {
     DEV_TOPK_TOO_LARGE = 1,        // 0 < k < V with k > KMAX
     DEV_ROUNDS_EXHAUSTED = 2,      // the exact walk needed more gather rounds than allowed
     DEV_INTERNAL = 3,
+    DEV_TIMEOUT = 4,               // a bounded wait ran out (the kernel returned early)
 };
 
 struct QsLaunch {
@@ -52,6 +53,8 @@ struct QsLaunch {
     int* status;                   // device word
     int n_s;                       // slice length per CTA (multiple of 8)
     int max_rounds;                // gather rounds allowed per row
+    const int32_t* rows;           // rows this launch serves, or null: all B rows
+    int nrows;                     // entries of rows
 };
 
 // Dynamic shared-memory layout; identical on host (sizing) and device.
