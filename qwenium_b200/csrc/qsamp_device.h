@@ -69,6 +69,7 @@ struct __align__(16) Misc {
     float red_f[NWARPS];
     int red_i[NWARPS];
     unsigned long long red_u[NWARPS];
+    unsigned long long red_u2[NWARPS];
     float cmax;            // this CTA's slice max
     int cmax_idx;
     float M;               // row max
@@ -78,6 +79,7 @@ struct __align__(16) Misc {
     int eq_count;          // elements equal to the selection key in this slice
     int sel_bin;           // broadcast radix bin
     int sel_rem;           // broadcast remaining rank
+    int sel_cnt;           // broadcast count of the chosen bin
     unsigned long long sel_remw;  // broadcast remaining weight (weighted select)
     float S_n, S_c;        // exact sums (broadcast)
     int first_round;

@@ -47,6 +47,17 @@ __device__ unsigned long long qs_phase[8192][24];
     do {                          \
     } while (0)
 #endif
+#ifdef QS_PHASE_TIMING
+#define QS_CYC(var) long long var = clock64()
+#define QS_ACC(acc, from) acc += clock64() - from
+#else
+#define QS_CYC(var) \
+    do {            \
+    } while (0)
+#define QS_ACC(acc, from) \
+    do {                  \
+    } while (0)
+#endif
 
 namespace qs {
 
@@ -1816,24 +1827,27 @@ __global__ void qs_softcap_lut_kernel(float* lut, float cap) {
 
 // ============================================================ streaming kernel
 // Greedy rows and top-k rows (k <= KMAX) with a short penalty window: one CTA
-// per row, the row streamed from HBM once in 8-element groups, two CTAs per
+// per row, the row streamed from HBM once in 2048-element chunks, two CTAs per
 // SM. Top-k keeps a candidate buffer under an exact threshold: an element
-// enters iff its (value, -id) composite beats the k-th best composite seen so
-// far, so the final top-k (value desc, id asc) is always among the kept ones.
+// enters iff its (value, -id) composite beats the k-th best composite of the
+// last compaction, so the final top-k (value desc, id asc) is always among the
+// kept ones. The threshold is also carried back to the raw logit (the row
+// transform is monotone), so most elements cost one compare.
 constexpr int SN_NT = 512;
-constexpr int SN_CH = 2048;                // elements per ring stage
-constexpr int SN_PER = SN_CH / SN_NT;      // elements per thread per stage
-constexpr int SN_CAP = KMAX + SN_CH;       // candidate buffer entries
+constexpr int SN_CH = 2048;                // elements per chunk
+constexpr int SN_PER = SN_CH / SN_NT;      // consecutive elements per thread per chunk
+constexpr int SN_CAP = KMAX + 2 * SN_CH;   // candidate buffer entries
+constexpr int SN_SLACK = 256;              // compaction once k + SN_SLACK are held
 constexpr int SN_HMAX = 1024;              // penalty window this kernel takes
-constexpr int SN_RING = 32768;             // ring bytes (4 fp32 / 8 bf16 stages)
-constexpr int SN_MAXST = 8;
 constexpr int SN_HT = 2 * SN_HMAX;         // window hash table slots (power of two)
+static_assert(SN_PER == 4 && SN_CAP % SN_NT == 0, "stream kernel shape");
+static_assert(KMAX + SN_SLACK + SN_CH + SN_HMAX <= SN_CAP, "candidate buffer bound");
 
 struct SnLayout {
-    int off_cand, off_hist, off_uid, off_ucnt, off_ring, off_bar, off_bitmap, off_misc, total;
+    int off_cand, off_hist, off_uid, off_ucnt, off_tail, off_bitmap, off_misc, total;
 };
 // uid/ucnt: the window's hash table (ids, counts), then the tail's scratch;
-// the ring doubles as the tail's t and cp scratch once the row is streamed.
+// tail: the exact tail's t (KMAX floats) and cp (KMAX doubles).
 __host__ __device__ inline SnLayout sn_layout(int V) {
     SnLayout L;
     int o = 0;
@@ -1841,67 +1855,74 @@ __host__ __device__ inline SnLayout sn_layout(int V) {
     L.off_hist = o;   o = align_up(o + 256 * 4, 16);
     L.off_uid = o;    o = align_up(o + SN_HT * 4, 16);
     L.off_ucnt = o;   o = align_up(o + SN_HT * 4, 16);
-    L.off_ring = o;   o = align_up(o + SN_RING, 128);
-    L.off_bar = o;    o = align_up(o + SN_MAXST * 8, 16);
+    L.off_tail = o;   o = align_up(o + KMAX * 12, 16);
     L.off_bitmap = o; o = align_up(o + ((V + 31) / 32) * 4, 16);
     L.off_misc = o;   o = align_up(o + (int)sizeof(Misc), 16);
     L.total = o;
     return L;
 }
 
-// ---- bulk-copy ring primitives (cp.async.bulk + mbarrier) ----
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(unsigned long long* b, uint32_t n) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(n) : "memory");
+__device__ __forceinline__ unsigned long long block_min_u64(unsigned long long v, Misc* m) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long y = __shfl_xor_sync(FULLMASK, v, o);
+        v = y < v ? y : v;
+    }
+    __syncthreads();
+    if (lane == 0) m->red_u[w] = v;
+    __syncthreads();
+    v = m->red_u[0];
+    for (int q = 1; q < NWARPS; ++q) v = m->red_u[q] < v ? m->red_u[q] : v;
+    __syncthreads();
+    return v;
 }
-__device__ __forceinline__ void mbar_arrive_tx(unsigned long long* b, uint32_t tx) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(tx) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(unsigned long long* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(unsigned long long* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded: a copy from valid global memory always lands; the limit only
-// turns a broken invariant into an error status instead of a hang.
-__device__ __forceinline__ bool mbar_wait(unsigned long long* b, uint32_t parity) {
-    for (int it = 0; it < (1 << 24); ++it)
-        if (mbar_try_wait(b, parity)) return true;
-    return false;
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, unsigned long long* b) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(b))
-                 : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
-// Exact k-th largest of n u64 values in a[] (8 radix rounds of 8 bits).
+// k-th largest of n distinct u64 keys (1 <= k <= n). Radix select on 8-bit
+// digits starting at the digit of the highest bit in which the keys differ
+// (candidate keys share their leading bytes), with warp-aggregated histogram
+// updates (lanes with the same digit add once), stopping as soon as the
+// chosen digit's bin holds exactly the remaining rank: the answer is then the
+// smallest key of that bin.
 __device__ unsigned long long block_kth_u64(const unsigned long long* a, int n, int k, uint32_t* hist, Misc* m) {
-    unsigned long long prefix = 0ull, mask = 0ull;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    unsigned long long ka = ~0ull, ko = 0ull;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) { ka &= a[i]; ko |= a[i]; }
+    for (int o = 16; o > 0; o >>= 1) {
+        ka &= __shfl_xor_sync(FULLMASK, ka, o);
+        ko |= __shfl_xor_sync(FULLMASK, ko, o);
+    }
+    __syncthreads();
+    if (lane == 0) { m->red_u[w] = ka; m->red_u2[w] = ko; }
+    __syncthreads();
+    ka = ~0ull;
+    ko = 0ull;
+    for (int q = 0; q < NWARPS; ++q) { ka &= m->red_u[q]; ko |= m->red_u2[q]; }
+    const unsigned long long diff = ka ^ ko;
+    if (diff == 0ull) return ka;  // a single distinct key
+    int shift = (63 - __clzll((long long)diff)) & ~7;
+    unsigned long long mask = shift + 8 < 64 ? (~0ull << (shift + 8)) : 0ull;
+    unsigned long long prefix = ka & mask;
     int rem = k;
-    for (int shift = 56; shift >= 0; shift -= 8) {
+    for (; shift >= 0; shift -= 8) {
+        __syncthreads();  // previous readers of hist, red_u and sel_* are done
         for (int d = threadIdx.x; d < 256; d += blockDim.x) hist[d] = 0u;
         __syncthreads();
-        for (int i = threadIdx.x; i < n; i += blockDim.x) {
-            const unsigned long long x = a[i];
-            if ((x & mask) == prefix) atomicAdd(&hist[(int)((x >> shift) & 255ull)], 1u);
+        for (int base = 0; base < n; base += blockDim.x) {
+            const int i = base + threadIdx.x;
+            const unsigned long long x = i < n ? a[i] : 0ull;
+            const bool act = i < n && (x & mask) == prefix;
+            const uint32_t am = __ballot_sync(FULLMASK, act);
+            if (act) {
+                const uint32_t d = (uint32_t)(x >> shift) & 255u;
+                const uint32_t peers = __match_any_sync(am, d);
+                if (lane == __ffs(peers) - 1) atomicAdd(&hist[d], (uint32_t)__popc(peers));
+            }
         }
         __syncthreads();
-        if (threadIdx.x < 32) {
-            const int lane = threadIdx.x;
-            int acc = 0, found = -1, left = rem;
-            for (int base = 255; base >= 0 && found < 0; base -= 32) {
-                const int d = base - lane;
+        if (w == 0) {
+            int acc = 0, found = -1, left = rem, cnt = 0;
+            for (int top = 255; top >= 0 && found < 0; top -= 32) {
+                const int d = top - lane;
                 const int c = (int)hist[d];
                 int pre = c;
                 for (int o = 1; o < 32; o <<= 1) {
@@ -1911,46 +1932,116 @@ __device__ unsigned long long block_kth_u64(const unsigned long long* a, int n, 
                 const uint32_t hm = __ballot_sync(FULLMASK, acc + pre >= rem);
                 if (hm) {
                     const int L = __ffs(hm) - 1;
-                    found = base - L;
-                    left = rem - (acc + __shfl_sync(FULLMASK, pre, L) - __shfl_sync(FULLMASK, c, L));
+                    found = top - L;
+                    cnt = __shfl_sync(FULLMASK, c, L);
+                    left = rem - (acc + __shfl_sync(FULLMASK, pre, L) - cnt);
                 } else {
                     acc += __shfl_sync(FULLMASK, pre, 31);
                 }
             }
-            if (lane == 0) { m->sel_bin = found < 0 ? 0 : found; m->sel_rem = left; }
+            if (lane == 0) { m->sel_bin = found < 0 ? 0 : found; m->sel_rem = left; m->sel_cnt = cnt; }
         }
         __syncthreads();
         prefix |= (unsigned long long)m->sel_bin << shift;
         mask |= 255ull << shift;
         rem = m->sel_rem;
-        __syncthreads();
+        if (m->sel_cnt == rem) {
+            unsigned long long mn = ~0ull;
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const unsigned long long x = a[i];
+                if ((x & mask) == prefix && x < mn) mn = x;
+            }
+            return block_min_u64(mn, m);
+        }
     }
+    __syncthreads();
     return prefix;
 }
 
-// Keep the candidates >= the k-th best (exactly k remain); returns that composite.
+// Keep the candidates >= the k-th best (exactly k remain: keys are distinct);
+// returns that key. Survivors are read into registers, then written to the
+// front in any order (the buffer is an unordered set).
 __device__ unsigned long long sn_compact(unsigned long long* cand, int& n, int k, uint32_t* hist, Misc* m) {
     const unsigned long long ck = block_kth_u64(cand, n, k, hist, m);
+    const int lane = threadIdx.x & 31;
+    constexpr int J = SN_CAP / SN_NT;
+    unsigned long long keep[J];
+    uint32_t kf = 0u;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int i = j * SN_NT + threadIdx.x;
+        keep[j] = i < n ? cand[i] : 0ull;
+        if (i < n && keep[j] >= ck) kf |= 1u << j;
+    }
     if (threadIdx.x == 0) m->spec_n = 0;
     __syncthreads();
-    // survivors move to the front; the slots they take are at most their own
-    const int iters = (n + SN_NT - 1) / SN_NT;
-    for (int it = 0; it < iters; ++it) {
-        const int i = it * SN_NT + threadIdx.x;
-        const unsigned long long x = i < n ? cand[i] : 0ull;
-        const bool keep = i < n && x >= ck;
-        int tot = 0;
-        const int rk = block_excl_scan_int(keep ? 1 : 0, tot, m);
-        const int base = m->spec_n;
-        __syncthreads();
-        if (keep) cand[base + rk] = x;
-        __syncthreads();
-        if (threadIdx.x == 0) m->spec_n = base + tot;
-        __syncthreads();
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const bool f = (kf >> j) & 1u;
+        const uint32_t bal = __ballot_sync(FULLMASK, f);
+        if (bal) {
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&m->spec_n, __popc(bal));
+            base = __shfl_sync(FULLMASK, base, 0);
+            if (f) cand[base + __popc(bal & ((1u << lane) - 1u))] = keep[j];
+        }
     }
+    __syncthreads();
     n = m->spec_n;
     __syncthreads();
     return ck;
+}
+
+// The SN_PER consecutive elements from i0 (raw logits and bf16 bits).
+__device__ __forceinline__ void sn_load(const RowCtx& r, bool vec, int i0, int V, float (&x)[SN_PER],
+                                        uint32_t (&b)[SN_PER]) {
+    if (vec && i0 + SN_PER <= V) {
+        if (r.dtype == QSAMP_BF16) {
+            const uint2 q = __ldg((const uint2*)((const uint16_t*)r.rowp + i0));
+            b[0] = q.x & 0xffffu; b[1] = q.x >> 16; b[2] = q.y & 0xffffu; b[3] = q.y >> 16;
+#pragma unroll
+            for (int e = 0; e < SN_PER; ++e) x[e] = __uint_as_float(b[e] << 16);
+        } else {
+            const float4 q = __ldg((const float4*)((const float*)r.rowp + i0));
+            x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+#pragma unroll
+            for (int e = 0; e < SN_PER; ++e) b[e] = 0u;
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < SN_PER; ++e) {
+            const int i = i0 + e;
+            x[e] = 0.0f;
+            b[e] = 0u;
+            if (i < V) {
+                x[e] = raw_at(r, i);
+                if (r.dtype == QSAMP_BF16) b[e] = ((const uint16_t*)r.rowp)[i];
+            }
+        }
+    }
+}
+
+// Smallest raw logit that can still reach the transformed value tv, rounded
+// down with margin: the row transform (soft-cap, /T, canon) is monotone
+// non-decreasing, so x < bound implies transform(x) < tv. Every rounding on
+// the way (1/cap, x*inv, tanh, cap*t, v/T) is within 2^-23 relative; the
+// bound backs off by 2^-20 relative per step, plus 1e-37 absolute for
+// subnormals. A NaN bound disables the filter (no compare against NaN holds).
+__device__ float raw_lower_bound(const RowCtx& r, float tv) {
+    if (r.force_on || !(tv > -__int_as_float(0x7f800000))) return -__int_as_float(0x7f800000);
+    double s = (double)tv;
+    if (r.div_on) s *= (double)r.T;
+    s -= fabs(s) * 0x1p-20 + 1e-37;
+    if (r.cap_on) {
+        const double t = s / (double)r.cap;
+        if (t <= -1.0) return -__int_as_float(0x7f800000);
+        if (t >= 1.0) return __int_as_float(0x7f800000);
+        double y = atanh(t);
+        y -= fabs(y) * 0x1p-20 + 1e-37;
+        s = y * (double)r.cap;
+        s -= fabs(s) * 0x1p-20 + 1e-37;
+    }
+    return __double2float_rd(s);
 }
 
 __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
@@ -1960,34 +2051,24 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
     uint32_t* hist = (uint32_t*)(smem_raw + L.off_hist);
     int32_t* uid = (int32_t*)(smem_raw + L.off_uid);
     int32_t* ucnt = (int32_t*)(smem_raw + L.off_ucnt);
-    unsigned char* ring = smem_raw + L.off_ring;
-    unsigned long long* bars = (unsigned long long*)(smem_raw + L.off_bar);
-    float* tbuf = (float*)ring;                 // tail scratch (after streaming)
-    double* cpbuf = (double*)(ring + KMAX * 4);
+    float* tbuf = (float*)(smem_raw + L.off_tail);
+    double* cpbuf = (double*)(smem_raw + L.off_tail + KMAX * 4);
     uint32_t* bitmap = (uint32_t*)(smem_raw + L.off_bitmap);
     Misc* m = (Misc*)(smem_raw + L.off_misc);
     const int V = a.V;
     const int words = (V + 31) / 32;
     const float NEG_INF = -__int_as_float(0x7f800000);
     const int lane = threadIdx.x & 31;
-    const int esz = a.dtype == QSAMP_BF16 ? 2 : 4;
-    const int stage_bytes = SN_CH * esz;
-    const int nstages = SN_RING / stage_bytes;
     for (int w = threadIdx.x; w < words; w += SN_NT) bitmap[w] = 0u;
-    if (threadIdx.x == 0) {
-        for (int q = 0; q < SN_MAXST; ++q) mbar_init(&bars[q], 1);
-        fence_mbar_init();
-    }
-    __shared__ int sh_nuniq, sh_n, sh_abort;
+    __shared__ int sh_nuniq, sh_n;
     __shared__ unsigned long long sh_tau;
-    if (threadIdx.x == 0) sh_abort = 0;
+    __shared__ float sh_xthr;  // raw-logit filter derived from sh_tau
     __syncthreads();
-    unsigned long long ring_base = 0;  // chunks consumed by this CTA before the current row
 
     for (int ri = blockIdx.x; ri < a.nrows; ri += gridDim.x) {
         const int row = a.rows[ri];
         QS_TMARK(row, 0, true);
-        if (threadIdx.x == 0) { m->prm = a.params[row]; sh_nuniq = 0; sh_n = 0; sh_tau = 0ull; }
+        if (threadIdx.x == 0) { m->prm = a.params[row]; sh_nuniq = 0; sh_n = 0; sh_tau = 0ull; sh_xthr = -__int_as_float(0x7f800000); }
         __syncthreads();
         const qsamp_row_params& p = m->prm;
         RowCtx r;
@@ -2046,125 +2127,81 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
         const int nuniq = sh_nuniq;
         QS_TMARK(row, 1, true);
 
-        // stream the row once through the bulk-copy ring: thread 0 keeps
-        // nstages chunks in flight; every thread consumes SN_PER elements of
-        // each chunk from shared memory
+        // stream the row once: each thread takes SN_PER consecutive elements
+        // of every chunk; the next chunk's loads are in flight while the
+        // current one is filtered
         float bv = NEG_INF;
         int bi = 0x7fffffff;
-        const bool tma = a.vec_ok != 0;  // 16-byte aligned rows
+        const bool vec = a.vec_ok != 0;  // 16-byte aligned rows
         const int nchunks = (V + SN_CH - 1) / SN_CH;
-        auto issue = [&](int c) {
-            const unsigned long long g = ring_base + (unsigned long long)c;
-            const int st = (int)(g % (unsigned long long)nstages);
-            const int elems = min(SN_CH, V - c * SN_CH);
-            const uint32_t rb = (uint32_t)(elems * esz) & ~15u;
-            if (rb) {
-                mbar_arrive_tx(&bars[st], rb);
-                bulk_g2s(ring + st * stage_bytes, (const char*)r.rowp + (size_t)c * SN_CH * esz, rb, &bars[st]);
-            } else {
-                mbar_arrive(&bars[st]);
-            }
-        };
-        if (tma && threadIdx.x == 0)
-            for (int c = 0; c < nchunks && c < nstages; ++c) issue(c);
+        const int trig = min(k + SN_SLACK, SN_CAP - SN_CH);
+        const int j0 = SN_PER * threadIdx.x;
+        float xn[SN_PER];
+        uint32_t bn[SN_PER];
+        sn_load(r, vec, j0, V, xn, bn);
         for (int c = 0; c < nchunks; ++c) {
-            const unsigned long long g = ring_base + (unsigned long long)c;
-            const int st = (int)(g % (unsigned long long)nstages);
-            const int elems = min(SN_CH, V - c * SN_CH);
-            const int rb_elems = tma ? (int)(((uint32_t)(elems * esz) & ~15u) / (uint32_t)esz) : 0;
-            const int mslot = c == 10 ? 5 : (c == 60 ? 10 : -1);
-            if (mslot >= 0) QS_TMARK(row, mslot, true);
-            if (tma && !mbar_wait(&bars[st], (uint32_t)((g / (unsigned long long)nstages) & 1ull))) {
-                set_status(a.status, DEV_TIMEOUT);
-                sh_abort = 1;
-            }
-            if (mslot >= 0) QS_TMARK(row, mslot + 1, true);
-            const int j0 = SN_PER * threadIdx.x;  // first element of this thread in the chunk
             const int i0 = c * SN_CH + j0;
-            unsigned long long mine[SN_PER];
-            int nm = 0;
             float x[SN_PER];
             uint32_t b16[SN_PER];
-            if (j0 + SN_PER <= rb_elems) {
-                if (esz == 2) {
-                    const uint2 q = *(const uint2*)(ring + st * stage_bytes + j0 * 2);
-                    b16[0] = q.x & 0xffffu; b16[1] = q.x >> 16; b16[2] = q.y & 0xffffu; b16[3] = q.y >> 16;
 #pragma unroll
-                    for (int e = 0; e < SN_PER; ++e) x[e] = __uint_as_float(b16[e] << 16);
-                } else {
-                    const float4 q = *(const float4*)(ring + st * stage_bytes + j0 * 4);
-                    x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+            for (int e = 0; e < SN_PER; ++e) { x[e] = xn[e]; b16[e] = bn[e]; }
+            if (c + 1 < nchunks) sn_load(r, vec, i0 + SN_CH, V, xn, bn);
+            if (greedy) {
+                if (i0 < V) {
+                    const uint32_t pen_bits = nuniq ? (bitmap[i0 >> 5] >> (i0 & 31)) : 0u;
 #pragma unroll
-                    for (int e = 0; e < SN_PER; ++e) b16[e] = 0u;
+                    for (int e = 0; e < SN_PER; ++e) {
+                        const int i = i0 + e;
+                        if (i >= V) break;
+                        if ((pen_bits >> e) & 1u) continue;  // window ids: folded in after the stream
+                        const float v = post_value(r, pre_value(r, i, x[e], b16[e]));
+                        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+                    }
                 }
             } else {
+                // raw-domain filter first; the exact transform and composite
+                // only for elements that can still beat the k-th candidate
+                const float xt = sh_xthr;
+                uint32_t lm = 0u;
 #pragma unroll
-                for (int e = 0; e < SN_PER; ++e) {
-                    const int i = i0 + e;
-                    const bool in = j0 + e < elems;
-                    x[e] = 0.0f;
-                    b16[e] = 0u;
-                    if (in && j0 + e < rb_elems) {
-                        if (esz == 2) { b16[e] = ((const uint16_t*)(ring + st * stage_bytes))[j0 + e]; x[e] = __uint_as_float(b16[e] << 16); }
-                        else x[e] = ((const float*)(ring + st * stage_bytes))[j0 + e];
-                    } else if (in) {
-                        x[e] = raw_at(r, i);
-                        b16[e] = r.dtype == QSAMP_BF16 ? ((const uint16_t*)r.rowp)[i] : 0u;
+                for (int e = 0; e < SN_PER; ++e)
+                    if (i0 + e < V && !(x[e] < xt)) lm |= 1u << e;
+                bool over = false;
+                if (__any_sync(FULLMASK, lm != 0u)) {
+                    if (nuniq && lm) lm &= ~(bitmap[i0 >> 5] >> (i0 & 31));  // window ids: folded in later
+                    const unsigned long long tau = sh_tau;
+                    while (__any_sync(FULLMASK, lm != 0u)) {
+                        bool ok = false;
+                        unsigned long long cc = 0ull;
+                        if (lm) {
+                            const int e = __ffs((int)lm) - 1;
+                            lm &= lm - 1u;
+                            const float xv = e == 0 ? x[0] : (e == 1 ? x[1] : (e == 2 ? x[2] : x[3]));
+                            const uint32_t hv = e == 0 ? b16[0] : (e == 1 ? b16[1] : (e == 2 ? b16[2] : b16[3]));
+                            const float v = post_value(r, pre_value(r, i0 + e, xv, hv));
+                            cc = composite(v, i0 + e);
+                            ok = cc > tau;
+                        }
+                        const uint32_t bal = __ballot_sync(FULLMASK, ok);
+                        if (bal) {
+                            int base = 0;
+                            if (lane == 0) base = atomicAdd(&sh_n, __popc(bal));
+                            base = __shfl_sync(FULLMASK, base, 0);
+                            if (ok) cand[base + __popc(bal & ((1u << lane) - 1u))] = cc;
+                            over |= base + __popc(bal) > trig;
+                        }
                     }
                 }
-            }
-            if (j0 < elems) {
-                const uint32_t pen_bits = nuniq ? (bitmap[i0 >> 5] >> (i0 & 31)) : 0u;
-                const unsigned long long tau = sh_tau;
-#pragma unroll
-                for (int e = 0; e < SN_PER; ++e) {
-                    const int i = i0 + e;
-                    if (j0 + e >= elems) break;
-                    if ((pen_bits >> e) & 1u) continue;  // window ids: folded in after the stream
-                    const float v = post_value(r, pre_value(r, i, x[e], b16[e]));
-                    if (greedy) {
-                        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
-                    } else {
-                        const unsigned long long cc = composite(v, i);
-                        if (cc > tau) mine[nm++] = cc;
-                    }
-                }
-            }
-            if (!greedy) {
-                int pre = nm;
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(FULLMASK, pre, o);
-                    if (lane >= o) pre += y;
-                }
-                const int wtot = __shfl_sync(FULLMASK, pre, 31);
-                int wbase = 0;
-                if (lane == 31 && wtot) wbase = atomicAdd(&sh_n, wtot);
-                wbase = __shfl_sync(FULLMASK, wbase, 31);
-                const int my = wbase + pre - nm;
-                for (int e = 0; e < nm; ++e) cand[my + e] = mine[e];
-            }
-            if (mslot >= 0) QS_TMARK(row, mslot + 2, true);
-            __syncthreads();  // the stage is consumed
-            if (mslot >= 0) QS_TMARK(row, mslot + 3, true);
-            if (tma && threadIdx.x == 0 && c + nstages < nchunks) {
-                fence_proxy_async();
-                issue(c + nstages);
-            }
-            if (!greedy) {
-                int n = sh_n;
-                if (n > SN_CAP - SN_CH) {
+                // the appender that crossed the trigger knows it: the decision
+                // is the barrier's own OR, identical in every thread
+                if (__syncthreads_or(over)) {
+                    int n = sh_n;
                     const unsigned long long ck = sn_compact(cand, n, k, hist, m);
-                    if (threadIdx.x == 0) { sh_tau = ck; sh_n = n; }
+                    if (threadIdx.x == 0) { sh_tau = ck; sh_n = n; sh_xthr = raw_lower_bound(r, comp_val(ck)); }
                     __syncthreads();
-#ifdef QS_PHASE_TIMING
-                    if (threadIdx.x == 0) qs_phase[row][20] += 1;
-#endif
                 }
             }
-            if (mslot >= 0) QS_TMARK(row, mslot + 4, true);
         }
-        if (tma) ring_base += (unsigned long long)nchunks;
-        if (sh_abort) return;
 
         // the window ids, one thread each: penalties as sampling.cpp:124-135
         // plus the frequency / presence extension
