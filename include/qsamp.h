@@ -161,14 +161,25 @@ qsamp_status qsamp_keep_list_mask(const char* path, int32_t V, uint32_t* mask_ou
 /* AND two allow-masks word by word (pruning AND grammar). */
 qsamp_status qsamp_mask_and(const uint32_t* a, const uint32_t* b, int64_t words, uint32_t* out);
 
-/* Vocab-sharded selection (tensor-parallel output head). ----------------
- * Rank r holds logits[:, v_offset : v_offset + V_local] of a V_total vocab.
- * Step 1 (each rank): the local top-k (k <= 1024) after the row transform,
- * as (value, global id) pairs sorted by (value desc, id asc), plus the local
- * max. Step 2: an all-gather of the [B][k] candidates over the ranks (NCCL),
- * then qsamp_merge_topk on every rank: the global top-k of the union
- * (ties to the lower global id), top-p, softmax and the draw, exactly as the
- * unsharded path. Penalties use global ids (hist holds global ids). */
+/* Vocab-sharded selection (tensor-parallel output head). No counterpart in
+ * the reference (its sampler sees whole rows). ----------------------------
+ * Rank r holds logits[:, v_offset : v_offset + V_local] of a V_total vocab
+ * (local_batch->V = V_local, row_stride in local elements).
+ * Step 1, qsamp_shard_topk on each rank: the row transform (soft-cap, allow
+ * mask, penalties, /T) and the local top-k as (value, global id) pairs sorted
+ * by (value desc, id asc) into DEVICE cand_vals / cand_ids [B][k], padded with
+ * (-inf, -1). hist and force_token hold GLOBAL ids; masks cover the local
+ * slice (bit i <-> global id v_offset + i). Every temperature row needs
+ * 0 < top_k <= k and top_k < V_total (a full-vocabulary top-p is served by
+ * the unsharded path only: QSAMP_ERR_UNSUPPORTED); penalty windows <= 1024;
+ * 1 <= k <= 1024. u and the batch's outputs are not used.
+ * Step 2: an all-gather of the [B][k] blocks over the ranks (NCCL), giving
+ * DEVICE all_vals / all_ids [n_ranks][B][k] rank-major, then
+ * qsamp_merge_topk on every rank: the global top-k of the union (ties to the
+ * lower global id), top-p, softmax and the draw. With top_k > 0 the
+ * reference's top-p and softmax see only the top-k set (sampling.cpp:158-190),
+ * so the rows equal the unsharded path's bit for bit. params and u are HOST
+ * [B]; n_ranks * k <= 5120. Slices must not overlap. */
 qsamp_status qsamp_shard_topk(qsamp_ctx* ctx, const qsamp_batch* local_batch, int32_t v_offset,
                               int32_t V_total, int32_t k, float* cand_vals, int32_t* cand_ids,
                               void* stream);

@@ -2,6 +2,7 @@
 // soft-cap tables, launches, and the host-side allow-mask helpers.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdarg>
@@ -22,11 +23,10 @@ extern "C" size_t qs_stream_smem(int V);
 extern "C" cudaError_t qs_stream_attrs(size_t smem);
 extern "C" cudaError_t qs_stream_occupancy(size_t smem, int* blocks_per_sm);
 extern "C" cudaError_t qs_launch_stream(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st);
-extern "C" cudaError_t qs_launch_shard(const qs::QsLaunch* a, int clusters, int cl, size_t smem, int v_offset,
-                                       int k, float* cand_vals, int32_t* cand_ids, cudaStream_t st);
-extern "C" cudaError_t qs_launch_merge(int n_ranks, int B, int k, const float* vals, const int32_t* ids,
-                                       const qsamp_row_params* params, const double* u, unsigned long long off,
-                                       int32_t* out_ids, qsamp_row_result* out_res, cudaStream_t st);
+extern "C" size_t qs_merge_smem();
+extern "C" cudaError_t qs_merge_attrs(size_t smem);
+extern "C" cudaError_t qs_launch_merge(const qs::QsLaunch* a, const float* all_vals, const int32_t* all_ids,
+                                       int n_ranks, int kc, int grid, size_t smem, cudaStream_t st);
 
 namespace {
 
@@ -67,6 +67,7 @@ struct qsamp_ctx {
     DevBuf<int32_t> rows;          // row lists: streamed rows, then cluster rows
     std::vector<int32_t> h_rows;
     size_t stream_attr = 0;
+    bool merge_attr = false;
     DevBuf<int> status;
     DevBuf<float> luts;
     float lut_caps[qs::MAX_LUT] = {0, 0, 0, 0};
@@ -157,7 +158,9 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, Plan& out) {
     return QSAMP_OK;
 }
 
-qsamp_status validate(qsamp_ctx* c, const qsamp_batch* b) {
+// V_total > 0: a vocabulary shard (force_token is a global id, outputs are
+// the candidate arrays of qsamp_shard_topk, not the batch's).
+qsamp_status validate(qsamp_ctx* c, const qsamp_batch* b, int V_total = 0) {
     if (!b) return fail(c, QSAMP_ERR_INVALID_ARG, "batch: expected non-NULL");
     if (b->B < 0) return fail(c, QSAMP_ERR_INVALID_ARG, "B: expected >= 0, got %d", b->B);
     if (b->B == 0) return QSAMP_OK;
@@ -168,8 +171,9 @@ qsamp_status validate(qsamp_ctx* c, const qsamp_batch* b) {
     if (b->dtype != QSAMP_F32 && b->dtype != QSAMP_BF16)
         return fail(c, QSAMP_ERR_INVALID_ARG, "dtype: expected QSAMP_F32 or QSAMP_BF16, got %d", (int)b->dtype);
     if (!b->params) return fail(c, QSAMP_ERR_INVALID_ARG, "params: expected non-NULL");
-    if (!b->out_ids && !b->out_results)
+    if (V_total == 0 && !b->out_ids && !b->out_results)
         return fail(c, QSAMP_ERR_INVALID_ARG, "out_ids/out_results: expected at least one non-NULL");
+    const int vt = V_total > 0 ? V_total : b->V;
     if (b->top_cap < 0 || b->top_cap > qs::KMAX)
         return fail(c, QSAMP_ERR_INVALID_ARG, "top_cap: expected [0,%d], got %d", qs::KMAX, b->top_cap);
     if (b->top_cap > 0 && (!b->out_top_ids || !b->out_top_probs))
@@ -185,8 +189,8 @@ qsamp_status validate(qsamp_ctx* c, const qsamp_batch* b) {
         if (p.flags != 0) return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].flags: expected 0, got %d", r, p.flags);
         if (std::isnan(p.temperature))
             return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].temperature: expected a number, got NaN", r);
-        if (p.force_token < -1 || p.force_token >= b->V)
-            return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].force_token: expected -1 or [0,%d), got %d", r, b->V,
+        if (p.force_token < -1 || p.force_token >= vt)
+            return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].force_token: expected -1 or [0,%d), got %d", r, vt,
                         p.force_token);
         if (b->hist) {
             const int len = b->hist_len ? b->hist_len[r] : b->hist_stride;
@@ -269,7 +273,7 @@ qsamp_status qsamp_create(int32_t device, qsamp_ctx** out) {
     cudaSetDevice(device);
     cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
     cudaDeviceGetAttribute(&c->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-    cudaError_t e = c->status.ensure(1);
+    cudaError_t e = c->status.ensure(2);  // [0] status word, [1] row queue
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     cudaSetDevice(prev);
     if (e != cudaSuccess) {
@@ -305,11 +309,13 @@ void qsamp_destroy(qsamp_ctx* c) {
 
 const char* qsamp_last_error(const qsamp_ctx* c) { return c ? c->err.c_str() : "no context"; }
 
-static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream_t st) {
-    qsamp_status s = validate(c, b);
-    if (s != QSAMP_OK || b->B == 0) return s;
+// Uploads the per-row parameters, history lengths and uniforms, prepares the
+// bf16 soft-cap tables, clears the status word and row queue, and fills the
+// launch fields every selection kernel shares. b has been validated.
+static qsamp_status common_setup(qsamp_ctx* c, const qsamp_batch* b, cudaStream_t st, qs::QsLaunch& a) {
     const int B = b->B;
     cudaError_t e;
+    qsamp_status s;
     if ((e = c->params.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(params)");
     if ((e = c->results.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(results)");
     if ((e = cudaMemcpyAsync(c->params.p, b->params, sizeof(qsamp_row_params) * B, cudaMemcpyHostToDevice, st)) !=
@@ -332,7 +338,46 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     }
     s = ensure_luts(c, b, st);
     if (s != QSAMP_OK) return s;
-    if ((e = cudaMemsetAsync(c->status.p, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail(c, e, "status reset");
+    if ((e = cudaMemsetAsync(c->status.p, 0, 2 * sizeof(int), st)) != cudaSuccess) return cuda_fail(c, e, "status reset");
+
+    a = qs::QsLaunch{};
+    a.logits = b->logits;
+    a.dtype = (int)b->dtype;
+    a.B = B;
+    a.V = b->V;
+    a.row_stride = b->row_stride;
+    const size_t esz = b->dtype == QSAMP_BF16 ? 2 : 4;
+    a.vec_ok = ((uintptr_t)b->logits % 16 == 0) && ((size_t)b->row_stride * esz % 16 == 0);
+    a.params = c->params.p;
+    a.hist = b->hist;
+    a.hist_stride = b->hist_stride;
+    a.hist_len = d_hl;
+    a.masks = b->masks;
+    a.mask_stride = b->mask_stride;
+    a.u = d_u;
+    a.philox_offset = b->rng_offset;
+    a.luts = c->luts.p;
+    for (int q = 0; q < qs::MAX_LUT; ++q) a.lut_caps[q] = c->lut_caps[q];
+    a.results = b->out_results ? b->out_results : c->results.p;
+    a.out_ids = b->out_ids;
+    a.top_ids = b->top_cap > 0 ? b->out_top_ids : nullptr;
+    a.top_probs = b->top_cap > 0 ? b->out_top_probs : nullptr;
+    a.top_cap = b->top_cap;
+    a.status = c->status.p;
+    a.row_ctr = c->status.p + 1;
+    a.max_rounds = kMaxRounds;
+    return QSAMP_OK;
+}
+
+static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream_t st) {
+    qsamp_status s = validate(c, b);
+    if (s != QSAMP_OK || b->B == 0) return s;
+    const int B = b->B;
+    const size_t esz = b->dtype == QSAMP_BF16 ? 2 : 4;
+    cudaError_t e;
+    qs::QsLaunch a;
+    s = common_setup(c, b, st, a);
+    if (s != QSAMP_OK) return s;
 
     // Route rows: greedy rows and top-k rows (k <= 1024) with a penalty
     // window of at most 1024 ids stream through one CTA each; the rest (full
@@ -365,36 +410,21 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         }
         if (!st_ok) c->h_rows[(size_t)j++] = r, ++n_cluster;
     }
+    // Cluster rows are served from a queue in list order: the ones likely to
+    // need the most gather rounds go first (a top-p cutoff, deeper p first),
+    // so that they do not start last and set the kernel's length.
+    std::stable_sort(c->h_rows.begin() + n_stream, c->h_rows.begin() + n_stream + n_cluster, [&](int x, int y) {
+        auto key = [&](int r) {
+            const float tp = b->params[r].top_p;
+            return (tp > 0.0f && tp < 1.0f) ? tp : 0.0f;
+        };
+        return key(x) > key(y);
+    });
     if ((e = c->rows.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(rows)");
     if ((e = cudaMemcpyAsync(c->rows.p, c->h_rows.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice, st)) !=
         cudaSuccess)
         return cuda_fail(c, e, "copying row lists");
 
-    qs::QsLaunch a = {};
-    a.logits = b->logits;
-    a.dtype = (int)b->dtype;
-    a.B = B;
-    a.V = b->V;
-    a.row_stride = b->row_stride;
-    const size_t esz = b->dtype == QSAMP_BF16 ? 2 : 4;
-    a.vec_ok = ((uintptr_t)b->logits % 16 == 0) && ((size_t)b->row_stride * esz % 16 == 0);
-    a.params = c->params.p;
-    a.hist = b->hist;
-    a.hist_stride = b->hist_stride;
-    a.hist_len = d_hl;
-    a.masks = b->masks;
-    a.mask_stride = b->mask_stride;
-    a.u = d_u;
-    a.philox_offset = b->rng_offset;
-    a.luts = c->luts.p;
-    for (int q = 0; q < qs::MAX_LUT; ++q) a.lut_caps[q] = c->lut_caps[q];
-    a.results = b->out_results ? b->out_results : c->results.p;
-    a.out_ids = b->out_ids;
-    a.top_ids = b->top_cap > 0 ? b->out_top_ids : nullptr;
-    a.top_probs = b->top_cap > 0 ? b->out_top_probs : nullptr;
-    a.top_cap = b->top_cap;
-    a.status = c->status.p;
-    a.max_rounds = kMaxRounds;
     if (n_stream > 0) {
         if (sn_smem > c->stream_attr) {
             if ((e = qs_stream_attrs(sn_smem)) != cudaSuccess) return cuda_fail(c, e, "stream kernel attributes");
@@ -605,18 +635,164 @@ qsamp_status qsamp_mask_and(const uint32_t* a, const uint32_t* b, int64_t words,
 }
 
 // ---------------------------------------------------------------- sharded
+// Candidates per row exchanged between ranks (n_ranks * k) are held by one
+// CTA of the merge kernel.
+static constexpr int kMergeCap = 5120;
+
+static qsamp_status shard_locked(qsamp_ctx* c, const qsamp_batch* lb, int32_t v_offset, int32_t V_total, int32_t k,
+                                 float* cand_vals, int32_t* cand_ids, cudaStream_t st) {
+    if (!lb) return fail(c, QSAMP_ERR_INVALID_ARG, "local_batch: expected non-NULL");
+    if (lb->V < 1) return fail(c, QSAMP_ERR_INVALID_ARG, "V (local): expected >= 1, got %d", lb->V);
+    if (v_offset < 0) return fail(c, QSAMP_ERR_INVALID_ARG, "v_offset: expected >= 0, got %d", v_offset);
+    if ((long long)V_total < (long long)v_offset + lb->V)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "V_total: expected >= v_offset + V (%lld), got %d",
+                    (long long)v_offset + lb->V, V_total);
+    if (k < 1 || k > qs::KMAX) return fail(c, QSAMP_ERR_INVALID_ARG, "k: expected [1,%d], got %d", qs::KMAX, k);
+    if (!cand_vals || !cand_ids) return fail(c, QSAMP_ERR_INVALID_ARG, "cand_vals/cand_ids: expected non-NULL");
+    qsamp_status s = validate(c, lb, V_total);
+    if (s != QSAMP_OK || lb->B == 0) return s;
+    const int B = lb->B;
+    for (int r = 0; r < B; ++r) {
+        const qsamp_row_params& p = lb->params[r];
+        if (p.temperature > 0.0f && !(p.top_k > 0 && p.top_k <= k && p.top_k < V_total))
+            return fail(c, QSAMP_ERR_UNSUPPORTED,
+                        "params[%d].top_k: the sharded path serves 0 < top_k <= k (%d) and < V_total (%d), got %d "
+                        "(a full-vocabulary top-p needs the unsharded path)", r, k, V_total, p.top_k);
+        if (lb->hist) {
+            const int len = lb->hist_len ? lb->hist_len[r] : lb->hist_stride;
+            const bool pen = p.repetition_penalty != 1.0f || p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
+            const unsigned long long lbk = (unsigned long long)(long long)p.repetition_lookback;
+            const long long w = (long long)(lbk < (unsigned long long)len ? lbk : (unsigned long long)len);
+            if (pen && w > 1024)
+                return fail(c, QSAMP_ERR_UNSUPPORTED, "row %d: the sharded path serves penalty windows <= 1024, got %lld",
+                            r, w);
+        }
+    }
+    const size_t sn_smem = qs_stream_smem(lb->V);
+    if (c->max_dyn == 0) {
+        size_t stc = 0;
+        cudaError_t e0 = qs_kernel_static_smem(&stc);
+        if (e0 != cudaSuccess) return cuda_fail(c, e0, "cudaFuncGetAttributes");
+        c->max_dyn = (size_t)c->smem_optin - stc;
+    }
+    if (sn_smem > c->max_dyn)
+        return fail(c, QSAMP_ERR_UNSUPPORTED, "V (local) = %d: the shard's allow-bitmap does not fit shared memory",
+                    lb->V);
+    qs::QsLaunch a;
+    s = common_setup(c, lb, st, a);
+    if (s != QSAMP_OK) return s;
+    cudaError_t e;
+    c->h_rows.resize((size_t)B);
+    for (int r = 0; r < B; ++r) c->h_rows[(size_t)r] = r;
+    if ((e = c->rows.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(rows)");
+    if ((e = cudaMemcpyAsync(c->rows.p, c->h_rows.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice, st)) !=
+        cudaSuccess)
+        return cuda_fail(c, e, "copying row lists");
+    if (sn_smem > c->stream_attr) {
+        if ((e = qs_stream_attrs(sn_smem)) != cudaSuccess) return cuda_fail(c, e, "stream kernel attributes");
+        c->stream_attr = sn_smem;
+    }
+    int per_sm = 0;
+    if ((e = qs_stream_occupancy(sn_smem, &per_sm)) != cudaSuccess || per_sm <= 0)
+        return cuda_fail(c, e == cudaSuccess ? cudaErrorInvalidConfiguration : e, "stream kernel occupancy");
+    a.rows = c->rows.p;
+    a.nrows = B;
+    a.v_offset = v_offset;
+    a.V_total = V_total;
+    a.cand_vals = cand_vals;
+    a.cand_ids = cand_ids;
+    a.cand_k = k;
+    const int grid = B < per_sm * c->num_sms ? B : per_sm * c->num_sms;
+    if ((e = qs_launch_stream(&a, grid, sn_smem, st)) != cudaSuccess) return cuda_fail(c, e, "stream kernel launch");
+    c->ctr.calls += 1;
+    c->ctr.rows += (uint64_t)B;
+    c->ctr.logit_bytes += (uint64_t)B * (uint64_t)lb->V * (lb->dtype == QSAMP_BF16 ? 2 : 4);
+    return QSAMP_OK;
+}
+
 qsamp_status qsamp_shard_topk(qsamp_ctx* c, const qsamp_batch* lb, int32_t v_offset, int32_t V_total, int32_t k,
                               float* cand_vals, int32_t* cand_ids, void* stream) {
-    (void)lb; (void)v_offset; (void)V_total; (void)k; (void)cand_vals; (void)cand_ids; (void)stream;
-    return fail(c, QSAMP_ERR_UNSUPPORTED, "vocab-sharded selection is not built yet");
+    if (!c) return QSAMP_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> g(c->mu);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != c->device) cudaSetDevice(c->device);
+    qsamp_status s = shard_locked(c, lb, v_offset, V_total, k, cand_vals, cand_ids, (cudaStream_t)stream);
+    if (prev != c->device) cudaSetDevice(prev);
+    return s;
+}
+
+static qsamp_status merge_locked(qsamp_ctx* c, int32_t n_ranks, int32_t B, int32_t k, const float* all_vals,
+                                 const int32_t* all_ids, const qsamp_row_params* params, const double* u,
+                                 uint64_t rng_offset, int32_t* out_ids, qsamp_row_result* out_results,
+                                 cudaStream_t st) {
+    if (n_ranks < 1) return fail(c, QSAMP_ERR_INVALID_ARG, "n_ranks: expected >= 1, got %d", n_ranks);
+    if (B < 0) return fail(c, QSAMP_ERR_INVALID_ARG, "B: expected >= 0, got %d", B);
+    if (k < 1 || k > qs::KMAX) return fail(c, QSAMP_ERR_INVALID_ARG, "k: expected [1,%d], got %d", qs::KMAX, k);
+    if ((long long)n_ranks * k > kMergeCap)
+        return fail(c, QSAMP_ERR_UNSUPPORTED, "n_ranks * k: expected <= %d candidates per row, got %lld", kMergeCap,
+                    (long long)n_ranks * k);
+    if (B == 0) return QSAMP_OK;
+    if (!all_vals || !all_ids) return fail(c, QSAMP_ERR_INVALID_ARG, "all_vals/all_ids: expected non-NULL");
+    if (!params) return fail(c, QSAMP_ERR_INVALID_ARG, "params: expected non-NULL");
+    if (!out_ids && !out_results)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "out_ids/out_results: expected at least one non-NULL");
+    for (int r = 0; r < B; ++r) {
+        const qsamp_row_params& p = params[r];
+        if (p.flags != 0) return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].flags: expected 0, got %d", r, p.flags);
+        if (std::isnan(p.temperature))
+            return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].temperature: expected a number, got NaN", r);
+        if (p.temperature > 0.0f && !(p.top_k > 0 && p.top_k <= k))
+            return fail(c, QSAMP_ERR_INVALID_ARG, "params[%d].top_k: expected (0,%d] for a merged row, got %d", r, k,
+                        p.top_k);
+        if (u && !(u[r] >= 0.0 && u[r] < 1.0))
+            return fail(c, QSAMP_ERR_INVALID_ARG, "u[%d]: expected [0,1), got %g", r, u[r]);
+    }
+    cudaError_t e;
+    if ((e = c->params.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(params)");
+    if ((e = c->results.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(results)");
+    if ((e = cudaMemcpyAsync(c->params.p, params, sizeof(qsamp_row_params) * B, cudaMemcpyHostToDevice, st)) !=
+        cudaSuccess)
+        return cuda_fail(c, e, "copying params");
+    const double* d_u = nullptr;
+    if (u) {
+        if ((e = c->u.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(u)");
+        if ((e = cudaMemcpyAsync(c->u.p, u, sizeof(double) * B, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+            return cuda_fail(c, e, "copying u");
+        d_u = c->u.p;
+    }
+    if ((e = cudaMemsetAsync(c->status.p, 0, 2 * sizeof(int), st)) != cudaSuccess) return cuda_fail(c, e, "status reset");
+    qs::QsLaunch a = {};
+    a.B = B;
+    a.params = c->params.p;
+    a.u = d_u;
+    a.philox_offset = rng_offset;
+    a.results = out_results ? out_results : c->results.p;
+    a.out_ids = out_ids;
+    a.status = c->status.p;
+    const size_t smem = qs_merge_smem();
+    if (!c->merge_attr) {
+        if ((e = qs_merge_attrs(smem)) != cudaSuccess) return cuda_fail(c, e, "merge kernel attributes");
+        c->merge_attr = true;
+    }
+    const int grid = B < 2 * c->num_sms ? B : 2 * c->num_sms;
+    if ((e = qs_launch_merge(&a, all_vals, all_ids, n_ranks, k, grid, smem, st)) != cudaSuccess)
+        return cuda_fail(c, e, "merge kernel launch");
+    return QSAMP_OK;
 }
 
 qsamp_status qsamp_merge_topk(qsamp_ctx* c, int32_t n_ranks, int32_t B, int32_t k, const float* all_vals,
                               const int32_t* all_ids, const qsamp_row_params* params, const double* u,
                               uint64_t rng_offset, int32_t* out_ids, qsamp_row_result* out_results, void* stream) {
-    (void)n_ranks; (void)B; (void)k; (void)all_vals; (void)all_ids; (void)params; (void)u; (void)rng_offset;
-    (void)out_ids; (void)out_results; (void)stream;
-    return fail(c, QSAMP_ERR_UNSUPPORTED, "vocab-sharded selection is not built yet");
+    if (!c) return QSAMP_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> g(c->mu);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != c->device) cudaSetDevice(c->device);
+    qsamp_status s = merge_locked(c, n_ranks, B, k, all_vals, all_ids, params, u, rng_offset, out_ids, out_results,
+                                  (cudaStream_t)stream);
+    if (prev != c->device) cudaSetDevice(prev);
+    return s;
 }
 
 }  // extern "C"

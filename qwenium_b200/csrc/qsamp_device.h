@@ -55,6 +55,14 @@ struct QsLaunch {
     int max_rounds;                // gather rounds allowed per row
     const int32_t* rows;           // rows this launch serves, or null: all B rows
     int nrows;                     // entries of rows
+    int* row_ctr;                  // row queue of the cluster kernel (zero at launch), or null
+    // vocab-sharded selection: this launch holds logits [v_offset, v_offset + V)
+    // of a V_total vocabulary; hist ids and force_token are global ids
+    int v_offset;
+    int V_total;                   // 0: V (unsharded)
+    float* cand_vals;              // non-null: write each row's sorted local top-k here
+    int32_t* cand_ids;             //   [B][cand_k] values / global ids (-1: padding)
+    int cand_k;
 };
 
 // Dynamic shared-memory layout; identical on host (sizing) and device.
@@ -80,6 +88,7 @@ struct __align__(16) Misc {
     int sel_bin;           // broadcast radix bin
     int sel_rem;           // broadcast remaining rank
     int sel_cnt;           // broadcast count of the chosen bin
+    int next_ri;           // leading CTA: the cluster's next row-list entry
     unsigned long long sel_remw;  // broadcast remaining weight (weighted select)
     float S_n, S_c;        // exact sums (broadcast)
     int first_round;

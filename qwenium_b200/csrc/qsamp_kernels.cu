@@ -250,21 +250,89 @@ __device__ int block_excl_scan_int(int v, int& total, Misc* m) {
     return base + x - v;
 }
 
-// Bitonic sort of n (power of two) u64 keys, descending, by the whole block.
-__device__ void bitonic_desc(unsigned long long* a, int n) {
-    for (int k = 2; k <= n; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < n; i += NT) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const unsigned long long x = a[i], y = a[ixj];
-                    const bool desc = (i & k) == 0;
-                    if (desc ? (x < y) : (x > y)) { a[i] = y; a[ixj] = x; }
-                }
-            }
-            __syncthreads();
+// Bitonic sort of n (power of two) u64 keys, descending, by the whole block
+// (512 threads). Each thread holds E = n / 512 consecutive keys (E in 1..8;
+// E = 1 for n < 512, then only the first n threads hold keys) in registers:
+// stages with partner distance j < E compare within a thread, j < 32E across
+// lanes by shuffles, and only the wide stages go through shared memory.
+template <int J, int E>
+__device__ __forceinline__ void bitonic_reg_stage(unsigned long long (&v)[E], int base, int k) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        if ((e & J) == 0) {
+            const bool desc = ((base + e) & k) == 0;
+            const unsigned long long x = v[e], y = v[e | J];
+            if (desc ? (x < y) : (x > y)) { v[e] = y; v[e | J] = x; }
         }
     }
+}
+
+__device__ __forceinline__ unsigned long long keep_of(unsigned long long x, unsigned long long y, bool keep_max) {
+    return keep_max ? (x > y ? x : y) : (x < y ? x : y);
+}
+
+template <int E>
+__device__ void bitonic_desc_reg(unsigned long long* a, int n) {
+    const int T = n / E;  // threads holding keys: whole warps (n >= 32)
+    const int t = threadIdx.x;
+    const bool act = t < T;
+    const int base = t * E;
+    unsigned long long v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = act ? a[base + e] : 0ull;
+    for (int k = 2; k <= n; k <<= 1) {
+        // for partner distances j >= E the direction and the side are the
+        // same for all E keys of a thread: k > j >= E > e
+        const bool desc = (base & k) == 0;
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= 32 * E) {
+                // exchange through shared memory, key base + e at e * T + t
+                // (bank-conflict free; the natural order is restored at the end)
+                __syncthreads();
+                if (act) {
+#pragma unroll
+                    for (int e = 0; e < E; ++e) a[e * T + t] = v[e];
+                }
+                __syncthreads();
+                if (act) {
+                    const bool keep_max = ((base & j) == 0) == desc;
+                    const int pt = t ^ (j / E);
+#pragma unroll
+                    for (int e = 0; e < E; ++e) v[e] = keep_of(v[e], a[e * T + pt], keep_max);
+                }
+            } else if (j >= E) {
+                if (act) {
+                    const int lj = j / E;
+                    const bool keep_max = ((base & j) == 0) == desc;
+#pragma unroll
+                    for (int e = 0; e < E; ++e) v[e] = keep_of(v[e], __shfl_xor_sync(FULLMASK, v[e], lj), keep_max);
+                }
+            } else if constexpr (E > 1) {
+                if (!act) continue;
+                if (E >= 8 && j == 4) bitonic_reg_stage<(E >= 8 ? 4 : 1), E>(v, base, k);
+                else if (E >= 4 && j == 2) bitonic_reg_stage<(E >= 4 ? 2 : 1), E>(v, base, k);
+                else bitonic_reg_stage<1, E>(v, base, k);
+            }
+        }
+    }
+    __syncthreads();
+    if (act) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) a[base + e] = v[e];
+    }
+    __syncthreads();
+}
+
+// Entries [n, next power of two) must hold 0 (the smallest key); n <= 4096.
+__device__ void bitonic_desc(unsigned long long* a, int n) {
+    if (n < 32) {
+        for (int i = n + threadIdx.x; i < 32; i += blockDim.x) a[i] = 0ull;
+        n = 32;
+    }
+    if (n >= 8 * NT) bitonic_desc_reg<8>(a, n);
+    else if (n >= 4 * NT) bitonic_desc_reg<4>(a, n);
+    else if (n >= 2 * NT) bitonic_desc_reg<2>(a, n);
+    else bitonic_desc_reg<1>(a, n);
 }
 
 __device__ void bitonic_asc_i32(int32_t* a, int n) {
@@ -1706,7 +1774,9 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
     const float NEG_INF = -__int_as_float(0x7f800000);
 
     const int nrows = a.rows ? a.nrows : a.B;
-    for (int ri = cid; ri < nrows; ri += ncl) {
+    // cluster c starts with row c; later rows come from a queue (a.row_ctr,
+    // zero at launch) so that slow rows do not pile up on one cluster
+    for (int ri = cid; ri < nrows;) {
         const int row = a.rows ? a.rows[ri] : ri;
         if (threadIdx.x == 0) m->prm = a.params[row];
         __syncthreads();
@@ -1815,7 +1885,14 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
         }
         __syncthreads();
         QS_TMARK(row, 4, rank == 0);
+        if (a.row_ctr && rank == 0 && threadIdx.x == 0) {
+            // pushed into every CTA's own shared memory before the barrier:
+            // no CTA reads a peer after the cluster's last barrier
+            const int nx = ncl + atomicAdd(a.row_ctr, 1);
+            for (int q = 0; q < CL; ++q) peer(cl, &m->next_ri, q)[0] = nx;
+        }
         cl.sync();
+        ri = a.row_ctr ? m->next_ri : ri + ncl;
     }
 }
 
@@ -1823,6 +1900,54 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
 __global__ void qs_softcap_lut_kernel(float* lut, float cap) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < 65536) lut[i] = qs_softcap(qs_bf16_to_f32((uint16_t)i), cap);
+}
+
+// ============================================================ row finish
+// Greedy result: the first maximum (std::max_element, sampling.cpp:98-108).
+__device__ void finish_greedy(const QsLaunch& a, int row, float bv, int bidx) {
+    if (threadIdx.x == 0) {
+        qsamp_row_result res;
+        res.token = bidx;
+        res.position = 0;
+        res.n_keep = 1;
+        res.drew = 0;
+        res.sum_exp = 0.0f;
+        res.sum_keep = 0.0f;
+        res.max_logit = bv;
+        res.prob = 1.0f;
+        write_result(a, row, res);
+    }
+    if (a.top_ids)
+        for (int i = threadIdx.x; i < a.top_cap; i += blockDim.x) {
+            a.top_ids[(size_t)row * a.top_cap + i] = i == 0 ? bidx : -1;
+            a.top_probs[(size_t)row * a.top_cap + i] = i == 0 ? 1.0f : 0.0f;
+        }
+}
+
+// Top-p, softmax and draw over the k best composites, sorted (value desc,
+// id asc) in spec[0..k): sampling.cpp:168-193.
+__device__ void finish_sorted(const QsLaunch& a, int row, int k, const unsigned long long* spec, float* t, float* part,
+                              float* prob, double* cp, Misc* m) {
+    if (comp_val(spec[0]) == -__int_as_float(0x7f800000)) {
+        // every logit masked: the reference's weights are NaN; the first
+        // sorted id, no draw
+        if (threadIdx.x == 0) {
+            qsamp_row_result res = {};
+            res.token = comp_idx(spec[0]);
+            res.n_keep = k;
+            res.max_logit = -__int_as_float(0x7f800000);
+            res.prob = __int_as_float(0x7fc00000);
+            write_result(a, row, res);
+        }
+        if (a.top_ids)
+            for (int i = threadIdx.x; i < a.top_cap; i += blockDim.x) {
+                a.top_ids[(size_t)row * a.top_cap + i] = -1;
+                a.top_probs[(size_t)row * a.top_cap + i] = 0.0f;
+            }
+        __syncthreads();
+    } else {
+        exact_tail(a, row, k, spec, t, part, prob, cp, m);
+    }
 }
 
 // ============================================================ streaming kernel
@@ -2085,8 +2210,11 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
         r.cap_on = p.softcap > 0.0f;
         r.T = p.temperature;
         r.div_on = p.temperature > 0.0f && p.temperature != 1.0f;
-        r.force = p.force_token;
-        r.force_on = p.force_token >= 0 && p.force_token < V;
+        // force_token is a global id; in a vocab shard that does not hold it
+        // every local logit is -inf (no local index matches)
+        const int vt = a.V_total > 0 ? a.V_total : V;
+        r.force_on = p.force_token >= 0 && p.force_token < vt;
+        r.force = r.force_on ? p.force_token - a.v_offset : -1;
         r.mask = a.masks ? a.masks + (size_t)row * (size_t)a.mask_stride : nullptr;
         r.lut = nullptr;
         if (r.cap_on && a.dtype == QSAMP_BF16 && a.luts)
@@ -2107,8 +2235,9 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
             const int wlen = len > 0 ? (int)(lb < (unsigned long long)len ? lb : (unsigned long long)len) : 0;
             const int32_t* h = a.hist + (size_t)row * (size_t)a.hist_stride + (len - wlen);
             for (int j = threadIdx.x; j < wlen; j += SN_NT) {
-                const int32_t id = h[j];
-                if (id < 0 || id >= V) continue;
+                const long long lid = (long long)h[j] - (long long)a.v_offset;  // local index
+                if (lid < 0 || lid >= V) continue;
+                const int32_t id = (int32_t)lid;
                 uint32_t slot = ((uint32_t)id * 2654435761u) & (SN_HT - 1);
                 while (true) {
                     const int old = atomicCAS(&uid[slot], -1, id);
@@ -2238,53 +2367,97 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
         if (greedy) {
             int bidx;
             bv = block_reduce_max_idx(bv, bi, bidx, m);
-            if (threadIdx.x == 0) {
-                qsamp_row_result res;
-                res.token = bidx == 0x7fffffff ? 0 : bidx;
-                res.position = 0;
-                res.n_keep = 1;
-                res.drew = 0;
-                res.sum_exp = 0.0f;
-                res.sum_keep = 0.0f;
-                res.max_logit = bv;
-                res.prob = 1.0f;
-                write_result(a, row, res);
-            }
-            if (a.top_ids)
-                for (int i = threadIdx.x; i < a.top_cap; i += SN_NT) {
-                    a.top_ids[(size_t)row * a.top_cap + i] = i == 0 ? (bidx == 0x7fffffff ? 0 : bidx) : -1;
-                    a.top_probs[(size_t)row * a.top_cap + i] = i == 0 ? 1.0f : 0.0f;
+            if (a.cand_vals) {
+                for (int i = threadIdx.x; i < a.cand_k; i += SN_NT) {
+                    a.cand_vals[(size_t)row * a.cand_k + i] = i == 0 ? bv : NEG_INF;
+                    a.cand_ids[(size_t)row * a.cand_k + i] = i == 0 ? a.v_offset + (bidx == 0x7fffffff ? 0 : bidx) : -1;
                 }
+            } else {
+                finish_greedy(a, row, bv, bidx == 0x7fffffff ? 0 : bidx);
+            }
         } else {
             int n = sh_n;
             if (n > k) sn_compact(cand, n, k, hist, m);
             const int P2 = next_pow2(k);
-            for (int i = k + threadIdx.x; i < P2; i += SN_NT) cand[i] = 0ull;
+            for (int i = n + threadIdx.x; i < P2; i += SN_NT) cand[i] = 0ull;
             __syncthreads();
             bitonic_desc(cand, P2);
             QS_TMARK(row, 3, true);
-            if (comp_val(cand[0]) == NEG_INF) {
-                // every logit masked: the reference's weights are NaN; the first
-                // sorted id, no draw
-                if (threadIdx.x == 0) {
-                    qsamp_row_result res = {};
-                    res.token = comp_idx(cand[0]);
-                    res.n_keep = k;
-                    res.max_logit = NEG_INF;
-                    res.prob = __int_as_float(0x7fc00000);
-                    write_result(a, row, res);
+            if (a.cand_vals) {
+                // the local top-k in (value desc, id asc) order, global ids
+                for (int i = threadIdx.x; i < a.cand_k; i += SN_NT) {
+                    const bool in = i < n;
+                    a.cand_vals[(size_t)row * a.cand_k + i] = in ? comp_val(cand[i]) : NEG_INF;
+                    a.cand_ids[(size_t)row * a.cand_k + i] = in ? a.v_offset + comp_idx(cand[i]) : -1;
                 }
-                if (a.top_ids)
-                    for (int i = threadIdx.x; i < a.top_cap; i += SN_NT) {
-                        a.top_ids[(size_t)row * a.top_cap + i] = -1;
-                        a.top_probs[(size_t)row * a.top_cap + i] = 0.0f;
-                    }
                 __syncthreads();
             } else {
-                exact_tail(a, row, k, cand, tbuf, (float*)uid, (float*)ucnt, cpbuf, m);
+                finish_sorted(a, row, k, cand, tbuf, (float*)uid, (float*)ucnt, cpbuf, m);
             }
         }
         QS_TMARK(row, 4, true);
+        __syncthreads();
+    }
+}
+
+// ============================================================ shard merge
+// Vocab-sharded selection, step 2: row r's candidates from every rank
+// ([n_ranks][B][kc] values and global ids, the layout of an all-gather of
+// each rank's [B][kc] block) -> the global top-k by (value desc, global id
+// asc), then the same finish as the unsharded kernels. Each rank's list holds
+// its own top-k, so the union holds the global top-k and, with k > 0, top-p
+// and softmax only ever see those k (sampling.cpp:158-190): the merge is
+// exact. One CTA per row.
+struct MgLayout {
+    int off_cand, off_hist, off_t, off_part, off_prob, off_cp, off_misc, total;
+};
+__host__ __device__ inline MgLayout mg_layout() {
+    MgLayout L;
+    int o = 0;
+    L.off_cand = o;  o = align_up(o + SN_CAP * 8, 16);
+    L.off_hist = o;  o = align_up(o + 256 * 4, 16);
+    L.off_t = o;     o = align_up(o + KMAX * 4, 16);
+    L.off_part = o;  o = align_up(o + KMAX * 4, 16);
+    L.off_prob = o;  o = align_up(o + KMAX * 4, 16);
+    L.off_cp = o;    o = align_up(o + KMAX * 8, 16);
+    L.off_misc = o;  o = align_up(o + (int)sizeof(Misc), 16);
+    L.total = o;
+    return L;
+}
+
+__global__ void __launch_bounds__(SN_NT, 1) qs_merge_kernel(QsLaunch a, const float* all_vals, const int32_t* all_ids,
+                                                            int n_ranks, int kc) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const MgLayout L = mg_layout();
+    unsigned long long* cand = (unsigned long long*)(smem_raw + L.off_cand);
+    uint32_t* hist = (uint32_t*)(smem_raw + L.off_hist);
+    float* t = (float*)(smem_raw + L.off_t);
+    float* part = (float*)(smem_raw + L.off_part);
+    float* prob = (float*)(smem_raw + L.off_prob);
+    double* cp = (double*)(smem_raw + L.off_cp);
+    Misc* m = (Misc*)(smem_raw + L.off_misc);
+    const int ntot = n_ranks * kc;  // <= SN_CAP (checked by the host)
+    for (int row = blockIdx.x; row < a.B; row += gridDim.x) {
+        if (threadIdx.x == 0) m->prm = a.params[row];
+        __syncthreads();
+        const qsamp_row_params& p = m->prm;
+        const bool greedy = p.temperature <= 0.0f;
+        const int k = greedy ? 1 : p.top_k;  // 0 < k <= kc (checked by the host)
+        for (int i = threadIdx.x; i < ntot; i += SN_NT) {
+            const int rk = i / kc, j = i - rk * kc;
+            const size_t o = ((size_t)rk * (size_t)a.B + (size_t)row) * (size_t)kc + (size_t)j;
+            const int32_t id = all_ids[o];
+            cand[i] = id < 0 ? 0ull : composite(canon(all_vals[o]), id);  // padding sorts last
+        }
+        __syncthreads();
+        int n = ntot;
+        if (n > k) sn_compact(cand, n, k, hist, m);
+        const int P2 = next_pow2(k);
+        for (int i = n + threadIdx.x; i < P2; i += SN_NT) cand[i] = 0ull;
+        __syncthreads();
+        bitonic_desc(cand, P2);
+        if (greedy) finish_greedy(a, row, comp_val(cand[0]), comp_idx(cand[0]));
+        else finish_sorted(a, row, k, cand, t, part, prob, cp, m);
         __syncthreads();
     }
 }
@@ -2342,6 +2515,16 @@ extern "C" cudaError_t qs_launch_lut(float* lut, float cap, cudaStream_t st) {
 }
 
 extern "C" size_t qs_stream_smem(int V) { return (size_t)qs::sn_layout(V).total; }
+
+extern "C" size_t qs_merge_smem() { return (size_t)qs::mg_layout().total; }
+extern "C" cudaError_t qs_merge_attrs(size_t smem) {
+    return cudaFuncSetAttribute(qs::qs_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+extern "C" cudaError_t qs_launch_merge(const qs::QsLaunch* a, const float* all_vals, const int32_t* all_ids,
+                                       int n_ranks, int kc, int grid, size_t smem, cudaStream_t st) {
+    qs::qs_merge_kernel<<<grid, qs::SN_NT, smem, st>>>(*a, all_vals, all_ids, n_ranks, kc);
+    return cudaGetLastError();
+}
 
 extern "C" cudaError_t qs_stream_attrs(size_t smem) {
     return cudaFuncSetAttribute(qs::qs_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -12,14 +12,14 @@
 // __device__ array of QSAMP_STATIC_SCRATCH_BYTES (640 KiB). Every GPU
 // that loads libqsamp.so holds one copy until the process exits. It stages
 // the per-row parameters, history lengths, uniforms and results (up to
-// QSAMP_STATIC_MAX_ROWS rows), the device status word, and one bf16 soft-cap
-// table. A host pointer to it is obtained per device with
-// cudaGetSymbolAddress -- the array's name in host code is only a stand-in,
-// never a device address.
+// QSAMP_STATIC_MAX_ROWS rows), the device status word and the cluster
+// kernel's row queue, and one bf16 soft-cap table. A host pointer to it is
+// obtained per device with cudaGetSymbolAddress -- the array's name in host
+// code is only a stand-in, never a device address.
 //
 // Sharing rules: all calls on a device share the one array and it keeps the
 // previous call's contents. Each call rewrites everything it reads (the
-// status word is cleared, parameters and the soft-cap table are copied or
+// status word and row queue are cleared, parameters and the soft-cap table are copied or
 // rebuilt). Two calls whose work overlaps on the GPU (different streams, or
 // different host threads) race on the array and must be serialised by the
 // caller.
@@ -160,7 +160,7 @@ extern "C" qsamp_status qsamp_sample_static(const qsamp_batch* b, void* stream, 
     const int B = b->B;
 
     // the previous call's contents: clear the status, rewrite what is read
-    if ((e = cudaMemsetAsync(status, 0, sizeof(int), s)) != cudaSuccess ||
+    if ((e = cudaMemsetAsync(status, 0, 2 * sizeof(int), s)) != cudaSuccess ||
         (e = cudaMemcpyAsync(d_params, b->params, sizeof(qsamp_row_params) * B, cudaMemcpyHostToDevice, s)) !=
             cudaSuccess ||
         (b->hist && b->hist_len &&
@@ -227,6 +227,7 @@ extern "C" qsamp_status qsamp_sample_static(const qsamp_batch* b, void* stream, 
     a.top_probs = b->top_cap > 0 ? b->out_top_probs : nullptr;
     a.top_cap = b->top_cap;
     a.status = status;
+    a.row_ctr = status + 1;  // the cluster kernel's row queue
     a.n_s = qs::align_up((b->V + cl - 1) / cl, 8);
     a.max_rounds = kMaxRounds;
     const size_t smem = (size_t)qs::smem_layout(a.n_s).total;

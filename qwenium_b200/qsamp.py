@@ -310,6 +310,56 @@ class Context:
         self._check(self.lib.qsamp_sample(self.h, ctypes.byref(b), ctypes.c_void_p(stream)), "qsamp_sample")
         return out_results
 
+    def shard_topk(self, local_logits, params, v_offset: int, V_total: int, k: int, hist=None, hist_len=None,
+                   masks=None, cand_vals=None, cand_ids=None, stream=None):
+        """Vocab-sharded step 1 (qsamp_shard_topk): this rank's logits
+        [B][V_local] hold global ids [v_offset, v_offset + V_local). Returns
+        (cand_vals [B][k] float32, cand_ids [B][k] int32 global ids, -1 for
+        padding) on the logits' device. hist holds global ids; masks cover
+        the local slice (bit i <-> global id v_offset + i)."""
+        import torch
+
+        B = int(local_logits.shape[0])
+        if cand_vals is None:
+            cand_vals = torch.empty((B, k), dtype=torch.float32, device=local_logits.device)
+        if cand_ids is None:
+            cand_ids = torch.empty((B, k), dtype=torch.int32, device=local_logits.device)
+        dtype = QSAMP_BF16 if local_logits.dtype in (torch.bfloat16, torch.int16, torch.uint16) else QSAMP_F32
+        params = np.ascontiguousarray(params, ROW_PARAMS)
+        if hist_len is not None:
+            hist_len = np.ascontiguousarray(hist_len, np.int32)
+        if stream is None:
+            stream = torch.cuda.current_stream(local_logits.device).cuda_stream
+        mstride = int(masks.stride(0)) if masks is not None and masks.dim() == 2 else 0
+        b = self._batch(
+            local_logits.data_ptr(), dtype, B, int(local_logits.shape[1]), int(local_logits.stride(0)), params,
+            _dev_ptr(hist), int(hist.stride(0)) if hist is not None else 0, hist_len, _dev_ptr(masks), mstride, None,
+            0, None, None, None, None, 0,
+        )
+        self._check(self.lib.qsamp_shard_topk(self.h, ctypes.byref(b), int(v_offset), int(V_total), int(k),
+                                              _dev_ptr(cand_vals), _dev_ptr(cand_ids), ctypes.c_void_p(stream)),
+                    "qsamp_shard_topk")
+        return cand_vals, cand_ids
+
+    def merge_topk(self, all_vals, all_ids, params, u=None, rng_offset=0, out_ids=None, out_results=None,
+                   stream=None):
+        """Vocab-sharded step 2 (qsamp_merge_topk): all_vals / all_ids are the
+        all-gathered candidates [n_ranks][B][k] (CUDA tensors)."""
+        import torch
+
+        n_ranks, B, k = (int(x) for x in all_vals.shape)
+        params = np.ascontiguousarray(params, ROW_PARAMS)
+        if u is not None:
+            u = np.ascontiguousarray(u, np.float64)
+        if out_results is None:
+            out_results = torch.empty((B, ROW_RESULT.itemsize), dtype=torch.uint8, device=all_vals.device)
+        if stream is None:
+            stream = torch.cuda.current_stream(all_vals.device).cuda_stream
+        self._check(self.lib.qsamp_merge_topk(self.h, n_ranks, B, k, _dev_ptr(all_vals), _dev_ptr(all_ids),
+                                              _np_ptr(params), _np_ptr(u), int(rng_offset), _dev_ptr(out_ids),
+                                              _dev_ptr(out_results), ctypes.c_void_p(stream)), "qsamp_merge_topk")
+        return out_results
+
     def sample_host(self, logits: np.ndarray, params, hist=None, hist_len=None, masks=None, u=None, rng_offset=0,
                     top_cap=0, bf16=False):
         """Host-memory entry (qsamp_sample_host): numpy in, numpy out."""
