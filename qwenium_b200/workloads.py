@@ -109,6 +109,68 @@ def config2(seed: int = 2, B: int = 10, V: int = V_QWEN) -> dict:
                 masks=None, seeds=seeds, u=uniforms_for(seeds))
 
 
+# ---- C3: a grammar-constrained batch -----------------------------------
+# Ids of the two end-of-text strings in the synthetic vocabulary (the
+# positions they hold in Qwen2's vocabulary).
+EOT_ID = 151643   # "<|endoftext|>"
+IM_END_ID = 151645  # "<|im_end|>"
+
+# A JSON-object grammar written for this build in the reference's GBNF
+# dialect (src/sampling/grammar_vocab.cpp parse_impl). The dialect has no
+# bounded repetition, so nesting depth <= 3 comes from per-depth rules.
+JSON_GBNF = r"""
+root   ::= obj1 ws
+obj1   ::= "{" ws ( pair1 ( ws "," ws pair1 )* )? ws "}"
+pair1  ::= string ws ":" ws val1
+val1   ::= obj2 | arr2 | scalar
+obj2   ::= "{" ws ( pair2 ( ws "," ws pair2 )* )? ws "}"
+arr2   ::= "[" ws ( val2 ( ws "," ws val2 )* )? ws "]"
+pair2  ::= string ws ":" ws val2
+val2   ::= obj3 | arr3 | scalar
+obj3   ::= "{" ws ( pair3 ( ws "," ws pair3 )* )? ws "}"
+arr3   ::= "[" ws ( scalar ( ws "," ws scalar )* )? ws "]"
+pair3  ::= string ws ":" ws scalar
+scalar ::= string | number | "true" | "false" | "null"
+string ::= "\"" [^"\\]* "\""
+number ::= "-"? [0-9]+ ( "." [0-9]+ )?
+ws     ::= [ \t\n]*
+"""
+
+
+def config3_vocab(seed: int = 3, V: int = V_QWEN) -> list:
+    """256 single bytes, then V-256 random printable strings of 2-16 bytes,
+    with the two end-of-text strings at EOT_ID / IM_END_ID."""
+    rng = np.random.default_rng(seed)
+    strs = [bytes([i]) for i in range(256)]
+    n = V - 256
+    lens = rng.integers(2, 17, n)
+    chars = rng.integers(0x20, 0x7F, int(lens.sum())).astype(np.uint8).tobytes()
+    offs = np.concatenate([[0], np.cumsum(lens)])
+    strs += [chars[offs[i]:offs[i + 1]] for i in range(n)]
+    if V > IM_END_ID:
+        strs[EOT_ID] = b"<|endoftext|>"
+        strs[IM_END_ID] = b"<|im_end|>"
+    return strs
+
+
+def config3(masks: np.ndarray, force: np.ndarray, seed: int = 3, extensions: bool = True) -> dict:
+    """C2's logits and parameters for len(masks) rows, each row constrained by
+    one grammar state: masks [B][ceil(V/32)] allow-bits (the reference's
+    valid ids plus its EOS rules, sampling.cpp:62-75) and force [B] (the EOS
+    string id for a stuck grammar, sampling.cpp:40-60, else -1). Without
+    extensions the frequency / presence penalties are off (the reference has
+    neither)."""
+    B = int(masks.shape[0])
+    cfg = config2(seed, B=B)
+    cfg["name"] = f"config3-B{B}"
+    cfg["masks"] = np.ascontiguousarray(masks, np.uint32)
+    cfg["params"]["force_token"] = np.asarray(force, np.int32)
+    if not extensions:
+        cfg["params"]["frequency_penalty"] = 0.0
+        cfg["params"]["presence_penalty"] = 0.0
+    return cfg
+
+
 def config4(seed: int = 4, B: int = 256, V: int = V_GEMMA) -> dict:
     """Large vocab: bf16 logits ~N(0,4^2), soft-cap 30, T 1.0, top-p 0.9,
     top-k 0, repetition penalty 1.05 over 512-id histories."""
