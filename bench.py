@@ -126,6 +126,14 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
+def stream_rows(params, V_, window=HIST):
+    """Rows the library routes to the stream kernel (qsamp_api.cu's rule):
+    greedy rows and 0 < top_k <= 1024, top_k < V, with a penalty window of at
+    most 1024 ids; the rest go to the cluster kernel."""
+    T, k = params["temperature"], params["top_k"]
+    return (T <= 0) | ((k > 0) & (k <= 1024) & (k < V_) & (window <= 1024))
+
+
 def algorithmic_bytes_per_row(V_, hist_len, bytes_per_logit=4, mask=False):
     # logits + history ids + params/u/result (SURVEY 8d per-row figure)
     return V_ * bytes_per_logit + (((V_ + 31) // 32) * 4 if mask else 0) + 4 * hist_len + 64
@@ -172,26 +180,29 @@ def run_gpu(args):
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ctx.counters()["kernel_launches"]
     with ClockSampler(local) as clk:
         e0.record(stream)
         for i in range(args.steps):
             step(args.warmup + i)
         e1.record(stream)
         torch.cuda.synchronize()
+    gpu_launches = int(ctx.counters()["kernel_launches"] - launches0)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    # per-launch kernel time: the same loop with an event pair per launch
-    per = []
+    # per-kernel device time: the same steps with the library's own events
+    # around each kernel launch (on the launching stream)
+    ctx.set_kernel_timing(True)
+    per_stream, per_rows = [], []
     for i in range(min(args.steps, 20)):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
         step(i)
-        b.record(stream)
-        b.synchronize()
-        per.append(a.elapsed_time(b))
-    launch_ms = statistics.mean(per)
+        c = ctx.counters()
+        per_stream.append(c["last_stream_kernel_ms"])
+        per_rows.append(c["last_rows_kernel_ms"])
+    ctx.set_kernel_timing(False)
+    k_stream, k_rows = statistics.mean(per_stream), statistics.mean(per_rows)
     ms_t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
@@ -251,9 +262,14 @@ def run_gpu(args):
     if rank != 0:
         return
     peak, peak_kind = measured_peaks()
-    alg = algorithmic_bytes_per_row(V, HIST) * B
+    n_stream = int(stream_rows(cfg["params"], V).sum())
+    if k_rows >= k_stream:
+        kname, units, launch_ms = "qs_rows_kernel", B - n_stream, k_rows
+    else:
+        kname, units, launch_ms = "qs_stream_kernel", n_stream, k_stream
+    alg = algorithmic_bytes_per_row(V, HIST) * units
     achieved = alg / (launch_ms * 1e-3) / 1e9
-    traffic = ncu_traffic("config2-B256")
+    traffic = ncu_traffic(f"{kname}/config2-B256")
     ms_step = ms / args.steps
     out = {
         "metric": "sampled rows/s (batched token selection, B=256, V=151936)",
@@ -273,10 +289,12 @@ def run_gpu(args):
                    "l2": f"rotating {ncopies} input copies ({ncopies * bytes_one / 1e6:.0f} MB) > L2"},
         "e2e": {"value": round(e2e_rows_s, 1) if e2e_rows_s else None, "unit": "rows/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,
+        "gpu_launches": gpu_launches,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_kind,
-                     "bytes_per_launch": alg, "launch_ms": round(launch_ms, 4)},
+                     "kernel": kname, "rows_per_launch": units, "bytes_per_launch": alg,
+                     "launch_ms": round(launch_ms, 4),
+                     "kernels_ms": {"qs_stream_kernel": round(k_stream, 4), "qs_rows_kernel": round(k_rows, 4)}},
         "clocks": clk.summary(),
     }
     if b10:

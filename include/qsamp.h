@@ -188,12 +188,23 @@ qsamp_status qsamp_merge_topk(qsamp_ctx* ctx, int32_t n_ranks, int32_t B, int32_
                               const qsamp_row_params* params, const double* u, uint64_t rng_offset,
                               int32_t* out_ids, qsamp_row_result* out_results, void* stream);
 
-/* Counters since creation (observability). */
+/* Counters since creation (observability). No counterpart in the
+ * reference. kernel_launches counts every kernel this context launched
+ * (selection, merge, soft-cap tables). With kernel timing on, each selection
+ * kernel launch is bracketed by CUDA events on the call's stream and
+ * qsamp_get_counters waits for the last call's events and reports their
+ * device times (0 for a kernel the call did not launch); timing off (the
+ * default) records nothing and qsamp_get_counters never waits. */
 typedef struct qsamp_counters {
     uint64_t calls, rows, logit_bytes, gather_rounds;
     double last_call_us;
+    uint64_t kernel_launches;
+    double last_stream_kernel_ms; /* greedy / top-k rows, and vocab shards */
+    double last_rows_kernel_ms;   /* full-vocabulary rows (cluster kernel) */
+    double last_merge_kernel_ms;  /* qsamp_merge_topk */
 } qsamp_counters;
 qsamp_status qsamp_get_counters(const qsamp_ctx* ctx, qsamp_counters* out);
+qsamp_status qsamp_set_kernel_timing(qsamp_ctx* ctx, int32_t on);
 
 #ifdef __cplusplus
 }

@@ -82,6 +82,11 @@ struct qsamp_ctx {
     size_t attrs_smem = 0;
     size_t max_dyn = 0;    // largest dynamic shared memory a CTA of the kernel may use
     qsamp_counters ctr = {};
+    // optional per-kernel device timing: begin / end events of the stream,
+    // cluster and merge kernels of the last call
+    bool timing = false;
+    cudaEvent_t ev[6] = {};
+    bool ev_used[3] = {false, false, false};
 };
 
 namespace {
@@ -109,6 +114,19 @@ struct Plan {
 
 // Smallest cluster whose slices fit the per-CTA shared-memory limit; for
 // small batches, wider clusters while every row still gets its own cluster.
+// Kernel slots of the timing events.
+enum { T_STREAM = 0, T_ROWS = 1, T_MERGE = 2 };
+void t_begin(qsamp_ctx* c, int k, cudaStream_t st) {
+    if (c->timing) cudaEventRecord(c->ev[2 * k], st);
+}
+void t_end(qsamp_ctx* c, int k, cudaStream_t st) {
+    c->ctr.kernel_launches += 1;
+    if (c->timing) {
+        cudaEventRecord(c->ev[2 * k + 1], st);
+        c->ev_used[k] = true;
+    }
+}
+
 qsamp_status plan_for(qsamp_ctx* c, int B, int V, Plan& out) {
     if (c->max_dyn == 0) {
         size_t st = 0;
@@ -233,6 +251,7 @@ qsamp_status ensure_luts(qsamp_ctx* c, const qsamp_batch* b, cudaStream_t st) {
         if (slot < 0) continue;  // more than MAX_LUT caps: remaining rows compute tanh per element
         e = qs_launch_lut(c->luts.p + (size_t)slot * 65536, cap, st);
         if (e != cudaSuccess) return cuda_fail(c, e, "soft-cap table launch");
+        c->ctr.kernel_launches += 1;
         c->lut_caps[slot] = cap;
         c->lut_next = (slot + 1) % qs::MAX_LUT;
     }
@@ -302,6 +321,9 @@ void qsamp_destroy(qsamp_ctx* c) {
     c->h_masks.release();
     c->h_top_probs.release();
     c->h_results.release();
+    c->rows.release();
+    for (cudaEvent_t ev : c->ev)
+        if (ev) cudaEventDestroy(ev);
     if (c->stream) cudaStreamDestroy(c->stream);
     cudaSetDevice(prev);
     delete c;
@@ -378,6 +400,7 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     qs::QsLaunch a;
     s = common_setup(c, b, st, a);
     if (s != QSAMP_OK) return s;
+    for (bool& u : c->ev_used) u = false;
 
     // Route rows: greedy rows and top-k rows (k <= 1024) with a penalty
     // window of at most 1024 ids stream through one CTA each; the rest (full
@@ -437,8 +460,10 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         sa.rows = c->rows.p;
         sa.nrows = n_stream;
         const int grid = n_stream < per_sm * c->num_sms ? n_stream : per_sm * c->num_sms;
+        t_begin(c, T_STREAM, st);
         if ((e = qs_launch_stream(&sa, grid, sn_smem, st)) != cudaSuccess)
             return cuda_fail(c, e, "stream kernel launch");
+        t_end(c, T_STREAM, st);
     }
     if (n_cluster > 0) {
         Plan plan;
@@ -448,8 +473,10 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         ca.rows = c->rows.p + n_stream;
         ca.nrows = n_cluster;
         ca.n_s = plan.n_s;
+        t_begin(c, T_ROWS, st);
         e = qs_launch_rows(&ca, plan.clusters, plan.cl, plan.smem, st);
         if (e != cudaSuccess) return cuda_fail(c, e, "selection kernel launch");
+        t_end(c, T_ROWS, st);
     }
     c->ctr.calls += 1;
     c->ctr.rows += (uint64_t)B;
@@ -553,7 +580,43 @@ qsamp_status qsamp_sample_host(qsamp_ctx* c, const qsamp_batch* hb) {
 qsamp_status qsamp_get_counters(const qsamp_ctx* c, qsamp_counters* out) {
     if (!c || !out) return QSAMP_ERR_INVALID_ARG;
     *out = c->ctr;
+    if (c->timing) {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        if (prev != c->device) cudaSetDevice(c->device);
+        double* dst[3] = {&out->last_stream_kernel_ms, &out->last_rows_kernel_ms, &out->last_merge_kernel_ms};
+        for (int k = 0; k < 3; ++k) {
+            *dst[k] = 0.0;
+            float ms = 0.0f;
+            if (c->ev_used[k] && cudaEventSynchronize(c->ev[2 * k + 1]) == cudaSuccess &&
+                cudaEventElapsedTime(&ms, c->ev[2 * k], c->ev[2 * k + 1]) == cudaSuccess)
+                *dst[k] = ms;
+        }
+        if (prev != c->device) cudaSetDevice(prev);
+    }
     return QSAMP_OK;
+}
+
+qsamp_status qsamp_set_kernel_timing(qsamp_ctx* c, int32_t on) {
+    if (!c) return QSAMP_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> g(c->mu);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != c->device) cudaSetDevice(c->device);
+    qsamp_status s = QSAMP_OK;
+    if (on && !c->ev[0]) {
+        for (cudaEvent_t& ev : c->ev) {
+            cudaError_t e = cudaEventCreate(&ev);
+            if (e != cudaSuccess) {
+                s = cuda_fail(c, e, "cudaEventCreate");
+                break;
+            }
+        }
+    }
+    if (s == QSAMP_OK) c->timing = on != 0;
+    for (bool& u : c->ev_used) u = false;
+    if (prev != c->device) cudaSetDevice(prev);
+    return s;
 }
 
 // ---------------------------------------------------------------- masks
@@ -703,7 +766,10 @@ static qsamp_status shard_locked(qsamp_ctx* c, const qsamp_batch* lb, int32_t v_
     a.cand_ids = cand_ids;
     a.cand_k = k;
     const int grid = B < per_sm * c->num_sms ? B : per_sm * c->num_sms;
+    for (bool& u : c->ev_used) u = false;
+    t_begin(c, T_STREAM, st);
     if ((e = qs_launch_stream(&a, grid, sn_smem, st)) != cudaSuccess) return cuda_fail(c, e, "stream kernel launch");
+    t_end(c, T_STREAM, st);
     c->ctr.calls += 1;
     c->ctr.rows += (uint64_t)B;
     c->ctr.logit_bytes += (uint64_t)B * (uint64_t)lb->V * (lb->dtype == QSAMP_BF16 ? 2 : 4);
@@ -776,8 +842,11 @@ static qsamp_status merge_locked(qsamp_ctx* c, int32_t n_ranks, int32_t B, int32
         c->merge_attr = true;
     }
     const int grid = B < 2 * c->num_sms ? B : 2 * c->num_sms;
+    for (bool& u : c->ev_used) u = false;
+    t_begin(c, T_MERGE, st);
     if ((e = qs_launch_merge(&a, all_vals, all_ids, n_ranks, k, grid, smem, st)) != cudaSuccess)
         return cuda_fail(c, e, "merge kernel launch");
+    t_end(c, T_MERGE, st);
     return QSAMP_OK;
 }
 

@@ -104,6 +104,10 @@ class _Counters(ctypes.Structure):
         ("logit_bytes", ctypes.c_uint64),
         ("gather_rounds", ctypes.c_uint64),
         ("last_call_us", ctypes.c_double),
+        ("kernel_launches", ctypes.c_uint64),
+        ("last_stream_kernel_ms", ctypes.c_double),
+        ("last_rows_kernel_ms", ctypes.c_double),
+        ("last_merge_kernel_ms", ctypes.c_double),
     ]
 
 
@@ -147,6 +151,8 @@ def load(path: str = LIB_PATH):
                                      ctypes.c_uint64, _P, _P, _P]
     lib.qsamp_get_counters.restype = ctypes.c_int
     lib.qsamp_get_counters.argtypes = [_P, ctypes.POINTER(_Counters)]
+    lib.qsamp_set_kernel_timing.restype = ctypes.c_int
+    lib.qsamp_set_kernel_timing.argtypes = [_P, ctypes.c_int32]
     lib.qsamp_sample_static.restype = ctypes.c_int
     lib.qsamp_sample_static.argtypes = [ctypes.POINTER(_Batch), _P, ctypes.c_char_p, ctypes.c_size_t]
     _lib = lib
@@ -250,6 +256,10 @@ class Context:
     def _check(self, rc: int, what: str):
         if rc:
             raise QsampError(rc, f"{what}: {self.lib.qsamp_last_error(self.h).decode(errors='replace')}")
+
+    def set_kernel_timing(self, on: bool):
+        """Bracket each selection kernel with CUDA events (see counters())."""
+        self._check(self.lib.qsamp_set_kernel_timing(self.h, 1 if on else 0), "qsamp_set_kernel_timing")
 
     def counters(self) -> dict:
         c = _Counters()
