@@ -21,6 +21,7 @@
 #include "sampling.h"
 #include "grammar_vocab.h"
 #include "token-trie.h"
+#include "ref_access.h"
 
 #include <atomic>
 #include <cstdint>
@@ -33,34 +34,7 @@
 
 namespace {
 
-// ---- access to TemperatureSampler::gen_ ------------------------------------
-// [temp.explicit]/12: access checking does not apply to the names used in an
-// explicit instantiation, so &TemperatureSampler::gen_ may be named here.
-template <typename Tag>
-struct MemberPtr {
-    static typename Tag::type value;
-};
-template <typename Tag>
-typename Tag::type MemberPtr<Tag>::value;
-
-template <typename Tag, typename Tag::type P>
-struct StoreMemberPtr {
-    struct Filler {
-        Filler() { MemberPtr<Tag>::value = P; }
-    };
-    static Filler filler;
-};
-template <typename Tag, typename Tag::type P>
-typename StoreMemberPtr<Tag, P>::Filler StoreMemberPtr<Tag, P>::filler;
-
-struct GenTag {
-    typedef std::mt19937 qwenium::TemperatureSampler::*type;
-};
-template struct StoreMemberPtr<GenTag, &qwenium::TemperatureSampler::gen_>;
-
-std::mt19937& engine_of(qwenium::TemperatureSampler& s) {
-    return s.*(MemberPtr<GenTag>::value);
-}
+using qwref_access::engine_of;
 
 struct Vocab {
     std::vector<std::string> strs;

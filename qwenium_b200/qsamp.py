@@ -62,7 +62,8 @@ STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "UNSUPPORTED", 4: "DEVICE", 5
 EXPORTS = (
     "qsamp_create", "qsamp_destroy", "qsamp_last_error", "qsamp_sample", "qsamp_sample_host",
     "qsamp_pack_ids", "qsamp_grammar_mask", "qsamp_find_eos_string", "qsamp_keep_list_mask",
-    "qsamp_mask_and", "qsamp_shard_topk", "qsamp_merge_topk", "qsamp_get_counters", "qsamp_sample_static",
+    "qsamp_mask_and", "qsamp_shard_topk", "qsamp_merge_topk", "qsamp_get_counters", "qsamp_set_kernel_timing",
+    "qsamp_sample_static",
 )
 
 _P = ctypes.c_void_p

@@ -86,3 +86,19 @@ def test_keep_list_file(lib):
         qsamp.keep_list_mask(p, 64)
     with pytest.raises(qsamp.QsampError):
         qsamp.keep_list_mask(os.path.join(d, "missing.bin"), 64)
+
+
+def test_adapter_compiles_against_reference_headers(tmp_path):
+    """qwenium_b200/adapter/cuda_sampler.cpp is a qwenium::Sampler subclass:
+    it must compile against the reference's own src/sampling headers."""
+    import subprocess
+
+    inc = "/root/reference/src/sampling"
+    if not os.path.exists(os.path.join(inc, "sampling.h")):
+        pytest.skip("reference headers not present")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run(["g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-I", inc, "-I", os.path.join(root, "include"),
+                        "-c", os.path.join(root, "qwenium_b200", "adapter", "cuda_sampler.cpp"),
+                        "-o", str(tmp_path / "cuda_sampler.o")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert "warning" not in r.stderr, r.stderr
