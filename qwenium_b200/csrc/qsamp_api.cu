@@ -79,6 +79,8 @@ struct qsamp_ctx {
     DevBuf<float> h_top_probs;
     DevBuf<qsamp_row_result> h_results;
     cudaStream_t stream = nullptr;
+    cudaStream_t aux = nullptr;    // second stream of a call: the stream kernel beside the cluster kernel
+    cudaEvent_t fork = nullptr, join = nullptr;
     size_t attrs_smem = 0;
     size_t max_dyn = 0;    // largest dynamic shared memory a CTA of the kernel may use
     qsamp_counters ctr = {};
@@ -294,9 +296,12 @@ qsamp_status qsamp_create(int32_t device, qsamp_ctx** out) {
     cudaDeviceGetAttribute(&c->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
     cudaError_t e = c->status.ensure(2);  // [0] status word, [1] row queue
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming);
     cudaSetDevice(prev);
     if (e != cudaSuccess) {
-        delete c;
+        qsamp_destroy(c);  // releases whatever was created
         return QSAMP_ERR_CUDA;
     }
     *out = c;
@@ -324,6 +329,9 @@ void qsamp_destroy(qsamp_ctx* c) {
     c->rows.release();
     for (cudaEvent_t ev : c->ev)
         if (ev) cudaEventDestroy(ev);
+    if (c->fork) cudaEventDestroy(c->fork);
+    if (c->join) cudaEventDestroy(c->join);
+    if (c->aux) cudaStreamDestroy(c->aux);
     if (c->stream) cudaStreamDestroy(c->stream);
     cudaSetDevice(prev);
     delete c;
@@ -448,22 +456,15 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         cudaSuccess)
         return cuda_fail(c, e, "copying row lists");
 
-    if (n_stream > 0) {
-        if (sn_smem > c->stream_attr) {
-            if ((e = qs_stream_attrs(sn_smem)) != cudaSuccess) return cuda_fail(c, e, "stream kernel attributes");
-            c->stream_attr = sn_smem;
-        }
-        int per_sm = 0;
-        if ((e = qs_stream_occupancy(sn_smem, &per_sm)) != cudaSuccess || per_sm <= 0)
-            return cuda_fail(c, e == cudaSuccess ? cudaErrorInvalidConfiguration : e, "stream kernel occupancy");
-        qs::QsLaunch sa = a;
-        sa.rows = c->rows.p;
-        sa.nrows = n_stream;
-        const int grid = n_stream < per_sm * c->num_sms ? n_stream : per_sm * c->num_sms;
-        t_begin(c, T_STREAM, st);
-        if ((e = qs_launch_stream(&sa, grid, sn_smem, st)) != cudaSuccess)
-            return cuda_fail(c, e, "stream kernel launch");
-        t_end(c, T_STREAM, st);
+    // With both kinds of rows, the cluster kernel goes first on the caller's
+    // stream and the stream kernel runs beside it on the context's second
+    // stream: clusters of 8 CTAs leave SMs free, which the stream kernel's
+    // CTAs fill. The caller's stream then waits for both (fork / join events).
+    const bool both = n_stream > 0 && n_cluster > 0;
+    cudaStream_t st2 = both ? c->aux : st;
+    if (both) {
+        if ((e = cudaEventRecord(c->fork, st)) != cudaSuccess || (e = cudaStreamWaitEvent(st2, c->fork, 0)) != cudaSuccess)
+            return cuda_fail(c, e, "fork to the second stream");
     }
     if (n_cluster > 0) {
         Plan plan;
@@ -477,6 +478,27 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         e = qs_launch_rows(&ca, plan.clusters, plan.cl, plan.smem, st);
         if (e != cudaSuccess) return cuda_fail(c, e, "selection kernel launch");
         t_end(c, T_ROWS, st);
+    }
+    if (n_stream > 0) {
+        if (sn_smem > c->stream_attr) {
+            if ((e = qs_stream_attrs(sn_smem)) != cudaSuccess) return cuda_fail(c, e, "stream kernel attributes");
+            c->stream_attr = sn_smem;
+        }
+        int per_sm = 0;
+        if ((e = qs_stream_occupancy(sn_smem, &per_sm)) != cudaSuccess || per_sm <= 0)
+            return cuda_fail(c, e == cudaSuccess ? cudaErrorInvalidConfiguration : e, "stream kernel occupancy");
+        qs::QsLaunch sa = a;
+        sa.rows = c->rows.p;
+        sa.nrows = n_stream;
+        const int grid = n_stream < per_sm * c->num_sms ? n_stream : per_sm * c->num_sms;
+        t_begin(c, T_STREAM, st2);
+        if ((e = qs_launch_stream(&sa, grid, sn_smem, st2)) != cudaSuccess)
+            return cuda_fail(c, e, "stream kernel launch");
+        t_end(c, T_STREAM, st2);
+    }
+    if (both) {
+        if ((e = cudaEventRecord(c->join, st2)) != cudaSuccess || (e = cudaStreamWaitEvent(st, c->join, 0)) != cudaSuccess)
+            return cuda_fail(c, e, "join from the second stream");
     }
     c->ctr.calls += 1;
     c->ctr.rows += (uint64_t)B;

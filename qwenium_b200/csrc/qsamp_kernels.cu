@@ -554,6 +554,9 @@ __device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s)
 // Penalties over the window (sampling.cpp:124-135 plus the frequency /
 // presence extension): every CTA sorts the window ids, and the leader of
 // each run that falls in this slice recomputes its value.
+constexpr int PF_SLOTS = 2048;  // penalty hash slots: 2 x 2048 ints fit the HIST_MAX window area
+static_assert(2 * PF_SLOTS <= HIST_MAX, "penalty hash table exceeds the window area");
+
 __device__ void penalty_fixup(const RowCtx& r, const QsLaunch& a, const Sm& s) {
     const qsamp_row_params& p = *r.p;
     const bool rep_on = p.repetition_penalty != 1.0f;
@@ -566,20 +569,38 @@ __device__ void penalty_fixup(const RowCtx& r, const QsLaunch& a, const Sm& s) {
     if (w <= 0) return;
     const int start = len - w;
     const int32_t* h = a.hist + (size_t)r.row * (size_t)a.hist_stride + start;
-    // unique ids and their counts: a direct scan for short windows (no
-    // barriers), a sort for long ones
+    // unique ids of this CTA's range and their counts: an open-addressing
+    // hash table (PF_SLOTS ids + counts in the window area) for windows of
+    // up to 1024 ids, a sort for longer ones
     const bool sorted = w > 1024;
+    int32_t* ht_id = s.hist;
+    int32_t* ht_cnt = s.hist + PF_SLOTS;
     if (sorted) {
         const int P2 = next_pow2(w);
         for (int j = threadIdx.x; j < P2; j += NT) s.hist[j] = j < w ? h[j] : 0x7fffffff;
         __syncthreads();
         bitonic_asc_i32(s.hist, P2);
     } else {
-        for (int j = threadIdx.x; j < w; j += NT) s.hist[j] = h[j];
+        for (int q = threadIdx.x; q < PF_SLOTS; q += NT) { ht_id[q] = -1; ht_cnt[q] = 0; }
+        __syncthreads();
+        for (int j = threadIdx.x; j < w; j += NT) {
+            const int32_t id = h[j];
+            if (id < r.lo || id >= r.hi) continue;
+            uint32_t slot = ((uint32_t)id * 2654435761u) & (PF_SLOTS - 1);
+            while (true) {  // at most w <= PF_SLOTS / 2 distinct ids: a free slot exists
+                const int old = atomicCAS(&ht_id[slot], -1, id);
+                if (old == -1 || old == id) {
+                    atomicAdd(&ht_cnt[slot], 1);
+                    break;
+                }
+                slot = (slot + 1) & (PF_SLOTS - 1);
+            }
+        }
         __syncthreads();
     }
-    for (int j = threadIdx.x; j < w; j += NT) {
-        const int32_t id = s.hist[j];
+    const int nslots = sorted ? w : PF_SLOTS;
+    for (int j = threadIdx.x; j < nslots; j += NT) {
+        const int32_t id = sorted ? s.hist[j] : ht_id[j];
         if (id < r.lo || id >= r.hi) continue;
         int c = 0;
         if (sorted) {
@@ -587,10 +608,7 @@ __device__ void penalty_fixup(const RowCtx& r, const QsLaunch& a, const Sm& s) {
             c = 1;
             while (j + c < w && s.hist[j + c] == id) ++c;
         } else {
-            bool dup = false;
-            for (int q = 0; q < j && !dup; ++q) dup = s.hist[q] == id;
-            if (dup) continue;
-            for (int q = j; q < w; ++q) c += s.hist[q] == id;
+            c = ht_cnt[j];
         }
         const float raw = r.force_on ? 0.0f : raw_at(r, id);
         const uint32_t b16 = (!r.force_on && r.dtype == QSAMP_BF16) ? ((const uint16_t*)r.rowp)[id] : 0u;
