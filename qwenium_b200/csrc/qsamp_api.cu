@@ -81,6 +81,12 @@ struct qsamp_ctx {
     cudaStream_t stream = nullptr;
     cudaStream_t aux = nullptr;    // second stream of a call: the stream kernel beside the cluster kernel
     cudaEvent_t fork = nullptr, join = nullptr;
+    // host entry point: logits copied in row chunks on a copy stream, each
+    // chunk followed by a ready flag (a 4-byte copy from pinned memory)
+    cudaStream_t copy = nullptr;
+    cudaEvent_t copy_go = nullptr, copy_done = nullptr;
+    DevBuf<int> ready;
+    int* pinned_one = nullptr;
     size_t attrs_smem = 0;
     size_t max_dyn = 0;    // largest dynamic shared memory a CTA of the kernel may use
     qsamp_counters ctr = {};
@@ -299,6 +305,11 @@ qsamp_status qsamp_create(int32_t device, qsamp_ctx** out) {
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->copy, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->copy_go, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->copy_done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaHostAlloc((void**)&c->pinned_one, sizeof(int), cudaHostAllocDefault);
+    if (e == cudaSuccess) *c->pinned_one = 1;
     cudaSetDevice(prev);
     if (e != cudaSuccess) {
         qsamp_destroy(c);  // releases whatever was created
@@ -329,6 +340,11 @@ void qsamp_destroy(qsamp_ctx* c) {
     c->rows.release();
     for (cudaEvent_t ev : c->ev)
         if (ev) cudaEventDestroy(ev);
+    c->ready.release();
+    if (c->pinned_one) cudaFreeHost(c->pinned_one);
+    if (c->copy_go) cudaEventDestroy(c->copy_go);
+    if (c->copy_done) cudaEventDestroy(c->copy_done);
+    if (c->copy) cudaStreamDestroy(c->copy);
     if (c->fork) cudaEventDestroy(c->fork);
     if (c->join) cudaEventDestroy(c->join);
     if (c->aux) cudaStreamDestroy(c->aux);
@@ -399,7 +415,10 @@ static qsamp_status common_setup(qsamp_ctx* c, const qsamp_batch* b, cudaStream_
     return QSAMP_OK;
 }
 
-static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream_t st) {
+// ready / ready_rows: rows arrive while the kernels run (see qsamp_sample_host);
+// null: every row is resident when the kernels start.
+static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream_t st, const int* ready = nullptr,
+                                  int ready_rows = 0) {
     qsamp_status s = validate(c, b);
     if (s != QSAMP_OK || b->B == 0) return s;
     const int B = b->B;
@@ -408,6 +427,8 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     qs::QsLaunch a;
     s = common_setup(c, b, st, a);
     if (s != QSAMP_OK) return s;
+    a.ready = ready;
+    a.ready_rows = ready_rows;
     for (bool& u : c->ev_used) u = false;
 
     // Route rows: greedy rows and top-k rows (k <= 1024) with a penalty
@@ -444,7 +465,9 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     // Cluster rows are served from a queue in list order: the ones likely to
     // need the most gather rounds go first (a top-p cutoff, deeper p first),
     // so that they do not start last and set the kernel's length.
+    // When rows arrive in chunks, rows of earlier chunks go first.
     std::stable_sort(c->h_rows.begin() + n_stream, c->h_rows.begin() + n_stream + n_cluster, [&](int x, int y) {
+        if (ready_rows > 0 && x / ready_rows != y / ready_rows) return x / ready_rows < y / ready_rows;
         auto key = [&](int r) {
             const float tp = b->params[r].top_p;
             return (tp > 0.0f && tp < 1.0f) ? tp : 0.0f;
@@ -531,11 +554,42 @@ qsamp_status qsamp_sample_host(qsamp_ctx* c, const qsamp_batch* hb) {
     const size_t esz = hb->dtype == QSAMP_BF16 ? 2 : 4;
     qsamp_batch db = *hb;
     cudaError_t e;
+    // Large batches: the logits cross PCIe in row chunks on the copy stream
+    // while the kernels already run; a kernel takes a row once its chunk's
+    // ready flag is set (the flag copy follows the chunk's copy in stream
+    // order). Small batches: one copy before the kernels.
+    const size_t total_bytes = (size_t)B * V * esz;
+    const int nchunks = (B >= 32 && total_bytes >= ((size_t)16 << 20)) ? 16 : 1;
+    const int chunk_rows = (B + nchunks - 1) / nchunks;
+    const int* ready = nullptr;
     do {
         if ((e = c->h_logits.ensure((size_t)B * V * esz)) != cudaSuccess) break;
-        if ((e = cudaMemcpy2DAsync(c->h_logits.p, (size_t)V * esz, hb->logits, (size_t)hb->row_stride * esz,
-                                   (size_t)V * esz, (size_t)B, cudaMemcpyHostToDevice, st)) != cudaSuccess)
-            break;
+        if (nchunks == 1) {
+            if ((e = cudaMemcpy2DAsync(c->h_logits.p, (size_t)V * esz, hb->logits, (size_t)hb->row_stride * esz,
+                                       (size_t)V * esz, (size_t)B, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+                break;
+        } else {
+            if ((e = c->ready.ensure(nchunks)) != cudaSuccess) break;
+            if ((e = cudaMemsetAsync(c->ready.p, 0, sizeof(int) * nchunks, st)) != cudaSuccess) break;
+            // the copies start after the flags are cleared (and after the
+            // previous call's work on st, which read the staging buffer)
+            if ((e = cudaEventRecord(c->copy_go, st)) != cudaSuccess) break;
+            if ((e = cudaStreamWaitEvent(c->copy, c->copy_go, 0)) != cudaSuccess) break;
+            for (int j = 0; j < nchunks && e == cudaSuccess; ++j) {
+                const int r0 = j * chunk_rows;
+                const int nr = B - r0 < chunk_rows ? B - r0 : chunk_rows;
+                if (nr <= 0) break;
+                e = cudaMemcpy2DAsync((unsigned char*)c->h_logits.p + (size_t)r0 * V * esz, (size_t)V * esz,
+                                      (const unsigned char*)hb->logits + (size_t)r0 * hb->row_stride * esz,
+                                      (size_t)hb->row_stride * esz, (size_t)V * esz, (size_t)nr,
+                                      cudaMemcpyHostToDevice, c->copy);
+                if (e == cudaSuccess)
+                    e = cudaMemcpyAsync(c->ready.p + j, c->pinned_one, sizeof(int), cudaMemcpyHostToDevice, c->copy);
+            }
+            if (e != cudaSuccess) break;
+            if ((e = cudaEventRecord(c->copy_done, c->copy)) != cudaSuccess) break;
+            ready = c->ready.p;
+        }
         db.logits = c->h_logits.p;
         db.row_stride = V;
         if (hb->hist) {
@@ -570,7 +624,9 @@ qsamp_status qsamp_sample_host(qsamp_ctx* c, const qsamp_batch* hb) {
         if (prev != c->device) cudaSetDevice(prev);
         return cuda_fail(c, e, "staging host inputs");
     }
-    s = sample_locked(c, &db, st);
+    s = sample_locked(c, &db, st, ready, ready ? chunk_rows : 0);
+    // st waits for the copy stream (flags and chunks) in every case
+    if (ready) cudaStreamWaitEvent(st, c->copy_done, 0);
     if (s == QSAMP_OK) {
         do {
             if (hb->out_ids && (e = cudaMemcpyAsync(hb->out_ids, c->h_ids.p, sizeof(int32_t) * B,

@@ -63,6 +63,10 @@ struct QsLaunch {
     float* cand_vals;              // non-null: write each row's sorted local top-k here
     int32_t* cand_ids;             //   [B][cand_k] values / global ids (-1: padding)
     int cand_k;
+    // rows arrive while the kernels run (host entry point): row r may be read
+    // once ready[r / ready_rows] != 0; null: all rows are resident at launch
+    const int* ready;
+    int ready_rows;
 };
 
 // Dynamic shared-memory layout; identical on host (sizing) and device.

@@ -624,6 +624,29 @@ __device__ void penalty_fixup(const RowCtx& r, const QsLaunch& a, const Sm& s) {
 }
 
 // ------------------------------------------------------------ outputs
+// Wait until row `row` of the logits has arrived (a.ready, set by the copy
+// engine after each chunk's copy). Thread 0 polls with an acquire load and
+// backs off; the wait is bounded (about 3 s), after which the status reports
+// DEV_TIMEOUT and the row is processed anyway. Every thread of the CTA must
+// call it (it ends with a block barrier).
+__device__ void wait_ready(const QsLaunch& a, int row) {
+    if (!a.ready) return;
+    if (threadIdx.x == 0) {
+        const int* f = a.ready + row / a.ready_rows;
+        for (int it = 0;; ++it) {
+            int v;
+            asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if (v != 0) break;
+            if (it >= (1 << 24)) {
+                set_status(a.status, DEV_TIMEOUT);
+                break;
+            }
+            __nanosleep(200);
+        }
+    }
+    __syncthreads();
+}
+
 __device__ void write_result(const QsLaunch& a, int row, const qsamp_row_result& res) {
     a.results[row] = res;
     if (a.out_ids) a.out_ids[row] = res.token;
@@ -900,6 +923,37 @@ __device__ void topk_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
 }
 
 // ------------------------------------------------------------ full path
+// Gathering during a full-path pass: CTA 0 appends straight into its list
+// with shared-memory atomics; every other CTA stages its elements in its own
+// (otherwise unused) list and hands them over after the pass with one
+// remote reservation (flush_to_leader), instead of a remote atomic per warp.
+__device__ void append_staged(const Sm& s, bool want, unsigned long long comp) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t wm = __ballot_sync(FULLMASK, want);
+    if (!wm) return;
+    int base = 0;
+    if (lane == __ffs(wm) - 1) base = atomicAdd(&s.misc->spec_n, __popc(wm));
+    base = __shfl_sync(FULLMASK, base, __ffs(wm) - 1);
+    if (want) {
+        const int slot = base + __popc(wm & ((1u << lane) - 1u));
+        if (slot < SPEC_CAP) s.spec[slot] = comp;
+    }
+}
+// After a cluster barrier that follows the pass (CTA 0's own appends are
+// complete); the next cluster barrier publishes the copies to CTA 0.
+__device__ void flush_to_leader(cg::cluster_group& cl, int rank, const Sm& s) {
+    if (rank == 0) return;
+    __shared__ int fl_base;
+    const int n = s.misc->spec_n < SPEC_CAP ? s.misc->spec_n : SPEC_CAP;
+    if (threadIdx.x == 0) fl_base = n > 0 ? atomicAdd(peer(cl, &s.misc->spec_n, 0), n) : 0;
+    __syncthreads();
+    unsigned long long* dst = peer(cl, s.spec, 0);
+    for (int i = threadIdx.x; i < n; i += NT) {
+        const int slot = fl_base + i;
+        if (slot < SPEC_CAP) dst[slot] = s.spec[i];
+    }
+}
+
 __device__ void push_flags(cg::cluster_group& cl, const Sm& s) {
     // CTA 0 copies flag / gs / gc / scalars to every other CTA
     const int CL = cl.num_blocks();
@@ -1417,6 +1471,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 if (first) { s.tx_lo[b] = 0u; s.tx_hi[b] = 0u; }
             }
             for (int q = threadIdx.x; q < NB / 32; q += NT) s.tie[q] = 0u;
+            if (rank != 0 && threadIdx.x == 0) m->spec_n = 0;  // this CTA's staged count
             __syncthreads();
             unsigned long long tail_tx = 0ull;
             const int iters = (r.len + NT - 1) / NT;
@@ -1448,7 +1503,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         }
                     }
                 }
-                append_to_leader(cl, s, want, comp);
+                append_staged(s, want, comp);
             }
             if (first) {
                 for (int o = 16; o > 0; o >>= 1) tail_tx += __shfl_down_sync(FULLMASK, tail_tx, o);
@@ -1467,7 +1522,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     const bool isq = i < r.len && s.vals[i] == NEG_INF;
                     int tot = 0;
                     const int rk = block_excl_scan_int(isq ? 1 : 0, tot, m);
-                    append_to_leader(cl, s, isq && taken + rk < quota, composite(NEG_INF, r.lo + i));
+                    append_staged(s, isq && taken + rk < quota, composite(NEG_INF, r.lo + i));
                     taken += tot;
                 }
             }
@@ -1475,6 +1530,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
         __syncthreads();
         if (it_no < 5) QS_TMARK(r.row, 8 + 3 * it_no, rank == 0);
         cl.sync();
+        flush_to_leader(cl, rank, s);
         {
             const int kmode = m->kmode;
             cluster_reduce_bins(cl, s, false, kmode != 0, m->kfrom, m->kto, m->first_round != 0);
@@ -1822,6 +1878,7 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
                 if (a.lut_caps[q] == p.softcap) r.lut = a.luts + (size_t)q * 65536;
         }
 
+        wait_ready(a, row);
         QS_TMARK(row, 0, rank == 0);
         transform_slice(r, a, s);
         __syncthreads();
@@ -2210,6 +2267,7 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
 
     for (int ri = blockIdx.x; ri < a.nrows; ri += gridDim.x) {
         const int row = a.rows[ri];
+        wait_ready(a, row);
         QS_TMARK(row, 0, true);
         if (threadIdx.x == 0) { m->prm = a.params[row]; sh_nuniq = 0; sh_n = 0; sh_tau = 0ull; sh_xthr = -__int_as_float(0x7f800000); }
         __syncthreads();

@@ -113,6 +113,13 @@ def test_host_entry_point(ctx, oracle_mod):
     check(ctx, oracle_mod, W.config2(22, B=6), host=True)
 
 
+def test_host_entry_point_chunked(ctx, oracle_mod):
+    """B=64 x 608 KB: the host entry copies the logits in 16 row chunks while
+    the kernels run (ready flags); two calls in a row reuse the flags."""
+    check(ctx, oracle_mod, W.config2(23, B=64), host=True)
+    check(ctx, oracle_mod, W.config2(24, B=80), host=True)
+
+
 def _edge_cfg(seed, V, B=12):
     rng = np.random.default_rng(seed)
     x = (rng.standard_normal((B, V)) * rng.uniform(0.5, 6)).astype(np.float32)
