@@ -954,33 +954,34 @@ __device__ void flush_to_leader(cg::cluster_group& cl, int rank, const Sm& s) {
     }
 }
 
-__device__ void push_flags(cg::cluster_group& cl, const Sm& s) {
-    // CTA 0 copies flag / gs / gc / scalars to every other CTA
-    const int CL = cl.num_blocks();
-    for (int q = 1; q < CL; ++q) {
-        uint32_t* df = (uint32_t*)peer(cl, s.flag, q);
-        uint32_t* dgs = (uint32_t*)peer(cl, (uint8_t*)s.gs, q);
-        uint32_t* dgc = (uint32_t*)peer(cl, (uint8_t*)s.gc, q);
-        const uint32_t* sf = (const uint32_t*)s.flag;
-        const uint32_t* sgs = (const uint32_t*)s.gs;
-        const uint32_t* sgc = (const uint32_t*)s.gc;
-        for (int w = threadIdx.x; w < NB / 4; w += NT) {
-            df[w] = sf[w];
-            dgs[w] = sgs[w];
-            dgc[w] = sgc[w];
-        }
-        if (threadIdx.x == 0) {
-            Misc* pm = peer(cl, s.misc, q);
-            pm->cmd = s.misc->cmd;
-            pm->first_round = s.misc->first_round;
-            pm->S_n = s.misc->S_n;
-            pm->cum_bmax = s.misc->cum_bmax;
-            pm->neg_quota = s.misc->neg_quota;
-            pm->kmode = s.misc->kmode;
-            pm->kfrom = s.misc->kfrom;
-            pm->kto = s.misc->kto;
-        }
+// After a cluster barrier that follows CTA 0's walk: every other CTA copies
+// CTA 0's bin flags, binade predictions and pass scalars into its own shared
+// memory (CTA 0 does not change them before the next barriers).
+__device__ void pull_flags(cg::cluster_group& cl, int rank, const Sm& s) {
+    if (rank == 0) return;
+    const Misc* pm = peer(cl, s.misc, 0);
+    // the pass reads the flags, and the binades of the k-sums it computes
+    const int kmode = pm->kmode;
+    const uint32_t* sf = (const uint32_t*)peer(cl, s.flag, 0);
+    const uint32_t* sg = (const uint32_t*)peer(cl, (uint8_t*)(kmode == 2 ? s.gc : s.gs), 0);
+    uint32_t* df = (uint32_t*)s.flag;
+    uint32_t* dg = (uint32_t*)(kmode == 2 ? s.gc : s.gs);
+    for (int w = threadIdx.x; w < NB / 4; w += NT) {
+        df[w] = sf[w];
+        if (kmode) dg[w] = sg[w];
     }
+    if (threadIdx.x == 0) {
+        Misc* m = s.misc;
+        m->cmd = pm->cmd;
+        m->first_round = pm->first_round;
+        m->S_n = pm->S_n;
+        m->cum_bmax = pm->cum_bmax;
+        m->neg_quota = pm->neg_quota;
+        m->kmode = pm->kmode;
+        m->kfrom = pm->kfrom;
+        m->kto = pm->kto;
+    }
+    __syncthreads();
 }
 
 // Exclusive prefix over bins of a per-bin value, by the whole CTA (NB = 4*NT).
@@ -1452,10 +1453,10 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
         __syncthreads();
         bool ovf = false;
         build_gather_set(s, -1, ovf);
-        push_flags(cl, s);
         QS_TMARK(r.row, 7, true);
     }
     cl.sync();
+    pull_flags(cl, rank, s);
     int it_no = 0;
 
     // command loop: every CTA runs CTA 0's pass; CTA 0 then walks
@@ -1824,11 +1825,11 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     __syncthreads();
                 }
             }
-            push_flags(cl, s);
             if (it_no < 5) QS_TMARK(r.row, 10 + 3 * it_no, true);
         }
         ++it_no;
         cl.sync();
+        pull_flags(cl, rank, s);
     }
 #ifdef QS_PHASE_TIMING
     if (threadIdx.x == 0 && rank == 0 && r.row < 8192) qs_phase[r.row][23] = (unsigned long long)it_no;
