@@ -42,6 +42,7 @@
 #define QS_DFMA(a, b, c) __fma_rn((a), (b), (c))
 #define QS_DDIV(a, b) __ddiv_rn((a), (b))
 #define QS_D2F(a) __double2float_rn(a)
+#define QS_FADD(a, b) __fadd_rn((a), (b))
 #define QS_TAB_EXP32 qs_tab_exp32_d
 #define QS_TAB_EXP64_HI qs_tab_exp64_hi_d
 #define QS_TAB_EXP64_LO qs_tab_exp64_lo_d
@@ -53,6 +54,7 @@
 #define QS_DFMA(a, b, c) fma((a), (b), (c))
 #define QS_DDIV(a, b) ((a) / (b))
 #define QS_D2F(a) ((float)(a))
+#define QS_FADD(a, b) ((a) + (b))
 #define QS_TAB_EXP32 qs_tab_exp32_h
 #define QS_TAB_EXP64_HI qs_tab_exp64_hi_h
 #define QS_TAB_EXP64_LO qs_tab_exp64_lo_h
@@ -251,5 +253,113 @@ QS_HD float qs_unkey(uint32_t k) {
 }
 
 QS_HD float qs_bf16_to_f32(uint16_t b) { return qs_u2f((uint32_t)b << 16); }
+
+// qs_run_add: c sequential float additions of the same term,
+//     for (i = 0; i < c; ++i) { S = S + t; if (S >= stop) return i; }  return c;
+// (round to nearest, ties to even) in O(1) per binade of S instead of O(c).
+// While the exact sum stays in S's binade [2^e, 2^(e+1)), S + t rounds to
+// S + rne(t / ulp) * ulp, so a run of equal terms adds a constant integer
+// k = rne(t / ulp) ulps -- except that when t / ulp is a half-integer n + 1/2
+// the rounding goes to the even neighbour: once S's mantissa is even every
+// add contributes n + (n & 1); an odd mantissa takes one single step first.
+// The add that leaves the binade, and operands outside the normal range, are
+// done as real float additions. Integer arithmetic on the encodings only, so
+// host and device agree bit for bit. S >= 0, t >= 0, stop >= 0 (or +inf).
+QS_HD long long qs_run_add(float* Sp, float t, long long c, float stop) {
+    float S = *Sp;
+    long long i = 0;
+    const uint32_t tb = qs_f2u(t);
+    const int et = (int)((tb >> 23) & 0xffu);
+    const uint64_t mt = et ? (uint64_t)((tb & 0x7fffffu) | 0x800000u) : (uint64_t)(tb & 0x7fffffu);
+    const int Et = (et ? et : 1) - 150;  /* t = mt * 2^Et */
+    const uint32_t pb = qs_f2u(stop);
+    const int stop_inf = ((pb >> 23) & 0xffu) == 0xffu;
+    const int ep = (int)((pb >> 23) & 0xffu);
+    const uint64_t mp = ep ? (uint64_t)((pb & 0x7fffffu) | 0x800000u) : (uint64_t)(pb & 0x7fffffu);
+    const int Ep = (ep ? ep : 1) - 150;  /* stop = mp * 2^Ep */
+    const uint64_t lim = 1ull << 24;
+    while (i < c) {
+        const uint32_t sb = qs_f2u(S);
+        const int es = (int)((sb >> 23) & 0xffu);
+        if (es == 0 || es >= 253 || tb == 0u) {
+            /* S zero or subnormal, near overflow, or t == 0: real adds (t == 0
+               leaves S unchanged: the first add decides) */
+            S = QS_FADD(S, t);
+            if (S >= stop) { *Sp = S; return i; }
+            ++i;
+            if (tb == 0u) { *Sp = S; return c; }
+            continue;
+        }
+        const uint64_t ms = (uint64_t)((sb & 0x7fffffu) | 0x800000u);
+        const int Es = es - 150; /* S = ms * 2^Es, ulp = 2^Es */
+        const int d = Es - Et;    /* t / ulp = mt * 2^-d */
+        uint64_t k;
+        int tie = 0;
+        uint64_t n;
+        if (d <= 0) {
+            if (-d >= 40) { S = QS_FADD(S, t); if (S >= stop) { *Sp = S; return i; } ++i; continue; }
+            n = mt << (-d);
+            k = n;
+        } else if (d >= 40) {
+            n = 0;
+            k = 0; /* t < 2^-16 ulp */
+        } else {
+            n = mt >> d;
+            const uint64_t rem = mt & ((1ull << d) - 1ull), half = 1ull << (d - 1);
+            tie = rem == half;
+            k = n + (rem > half ? 1u : 0u);
+        }
+        if (tie && (ms & 1u)) {
+            /* one step to an even mantissa */
+            const uint64_t r = ms + n + ((ms + n) & 1u);
+            if (r > lim) { S = QS_FADD(S, t); if (S >= stop) { *Sp = S; return i; } ++i; continue; }
+            S = r == lim ? qs_u2f((uint32_t)(es + 1) << 23) : qs_u2f(((uint32_t)es << 23) | (uint32_t)(r - 0x800000u));
+            if (S >= stop) { *Sp = S; return i; }
+            ++i;
+            continue;
+        }
+        if (tie) k = n + (n & 1u);
+        if (k == 0) { /* S never changes again */
+            *Sp = S;
+            return (S >= stop) ? i : c;
+        }
+        const uint64_t room = (lim - ms) / k;
+        if (room == 0) { /* the next add leaves the binade */
+            S = QS_FADD(S, t);
+            if (S >= stop) { *Sp = S; return i; }
+            ++i;
+            continue;
+        }
+        const uint64_t left = (uint64_t)(c - i);
+        const uint64_t nadd = room < left ? room : left;
+        if (!stop_inf) {
+            /* first j >= 1 with (ms + j k) 2^Es >= mp 2^Ep */
+            const int D2 = Ep - Es;
+            uint64_t T;
+            int never = 0;
+            if (D2 >= 0) {
+                if (D2 >= 40 || (mp << D2) > (1ull << 50)) never = 1;
+                T = never ? 0 : (mp << D2);
+            } else {
+                const int sh = -D2;
+                T = sh >= 63 ? (mp ? 1u : 0u) : ((mp + (1ull << sh) - 1ull) >> sh);
+            }
+            if (!never) {
+                const uint64_t j = T <= ms ? 1u : (T - ms + k - 1u) / k;
+                if (j <= nadd) {
+                    const uint64_t r = ms + j * k;
+                    S = r == lim ? qs_u2f((uint32_t)(es + 1) << 23) : qs_u2f(((uint32_t)es << 23) | (uint32_t)(r - 0x800000u));
+                    *Sp = S;
+                    return i + (long long)j - 1;
+                }
+            }
+        }
+        const uint64_t r = ms + nadd * k;
+        S = r == lim ? qs_u2f((uint32_t)(es + 1) << 23) : qs_u2f(((uint32_t)es << 23) | (uint32_t)(r - 0x800000u));
+        i += (long long)nadd;
+    }
+    *Sp = S;
+    return c;
+}
 
 #endif  // QS_MATH_H

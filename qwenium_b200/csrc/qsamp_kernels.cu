@@ -84,11 +84,18 @@ struct Sm {
     int8_t* gs;
     int8_t* gc;
     uint32_t* tie;
+    uint32_t* vmin;            // per bin: smallest / largest qs_key(value) (uniform bins: equal)
+    uint32_t* vmax;
     int32_t* hist;
     unsigned long long* spec;
     float* spect;
     Misc* misc;
 };
+
+__device__ __forceinline__ bool uniform_bin(const uint32_t* cnt, const uint32_t* vmin, const uint32_t* vmax, int b) {
+    return b < NB - 1 && cnt[b] > 0 && vmin[b] == vmax[b];
+}
+#define UNIFORM(b) uniform_bin(s.cnt, s.vmin, s.vmax, (b))
 
 __device__ __forceinline__ Sm carve(unsigned char* base, int n_s) {
     const SmemLayout L = smem_layout(n_s);
@@ -109,6 +116,8 @@ __device__ __forceinline__ Sm carve(unsigned char* base, int n_s) {
     s.gs = (int8_t*)(base + L.off_gs);
     s.gc = (int8_t*)(base + L.off_gc);
     s.tie = (uint32_t*)(base + L.off_tie);
+    s.vmin = (uint32_t*)(base + L.off_vmin);
+    s.vmax = (uint32_t*)(base + L.off_vmax);
     s.hist = (int32_t*)(base + L.off_hist);
     s.spec = (unsigned long long*)(base + L.off_spec);
     s.spect = (float*)(base + L.off_spect);
@@ -131,6 +140,12 @@ __device__ __forceinline__ float canon(float v) {
     if (v != v) return -__int_as_float(0x7f800000);
     return v == 0.0f ? 0.0f : v;
 }
+
+// A bin whose elements all hold one value (after the cluster reduction, on
+// CTA 0): the walks add its run of equal terms in closed form (qs_run_add),
+// so it never needs gathering for a sum, a binade crossing or a rounding tie.
+struct Sm;
+__device__ __forceinline__ bool uniform_bin(const uint32_t* cnt, const uint32_t* vmin, const uint32_t* vmax, int b);
 
 __device__ __forceinline__ int binof(float x) {
     // x <= 0; larger x -> lower bin. Monotone: rounding of -x*R preserves order.
@@ -1117,7 +1132,8 @@ struct WalkState {
 // bin never has to fit a gather list. Returns the id, how many elements of
 // the bin precede it, and its probability t / Sc.
 __device__ void leader_weighted_select(cg::cluster_group& cl, const Sm& s, int n_s, int V, int bsel, double R_t,
-                                       float M, float Sc, int& out_id, long long& out_before, float& out_prob) {
+                                       float M, float Sc, long long max_rank, int& out_id, long long& out_before,
+                                       float& out_prob) {
     const int CL = cl.num_blocks();
     const float NEG_INF = -__int_as_float(0x7f800000);
     unsigned long long* hw = s.ksum;
@@ -1195,6 +1211,8 @@ __device__ void leader_weighted_select(cg::cluster_group& cl, const Sm& s, int n
     long long pos = wK > 0 ? (long long)((ws_R + wK - 1) / wK) - 1 : 0;
     if (pos < 0) pos = 0;
     if (pos > (long long)ws_cntK - 1) pos = (long long)ws_cntK - 1;
+    if (ws_before + pos > max_rank) pos = max_rank - ws_before;  // the cut bin: survivors only
+    if (pos < 0) pos = 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int chunk = (V + NWARPS - 1) / NWARPS;
     const int c0 = warp * chunk, c1 = min(V, c0 + chunk);
@@ -1256,13 +1274,18 @@ __device__ void cluster_reduce_bins(cg::cluster_group& cl, const Sm& s, bool cnt
     const int b0 = rank * per;
     for (int b = b0 + threadIdx.x; b < b0 + per; b += NT) {
         if (cnt_tsum) {
-            uint32_t c = 0;
+            uint32_t c = 0, lo = 0xffffffffu, hi = 0u;
             unsigned long long t = 0;
             for (int q = 0; q < CL; ++q) {
                 c += peer(cl, s.cnt, q)[b];
                 t += peer(cl, s.tsum32, q)[b];
+                const uint32_t a0 = peer(cl, s.vmin, q)[b], a1 = peer(cl, s.vmax, q)[b];
+                lo = a0 < lo ? a0 : lo;
+                hi = a1 > hi ? a1 : hi;
             }
             peer(cl, s.cnt, 0)[b] = c;
+            peer(cl, s.vmin, 0)[b] = lo;
+            peer(cl, s.vmax, 0)[b] = hi;
             peer(cl, s.tsum, 0)[b] = b < NB - 1 ? (float)((double)t * (double)tsum_scale(b)) : 0.0f;
         }
         if (ks && b >= kfrom && b <= kto) {
@@ -1304,8 +1327,8 @@ __device__ void predict_s(const Sm& s, int from, double ratio) {
         if (b >= from && b < NB - 1 && s.cnt[b] > 0) {
             const double Pa = s.pref[b] * ratio, Pb = (s.pref[b] + (double)TX(b) * 0x1p-40) * ratio;
             const bool want = b == from || !(Pa > 0.0) || binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
-            if (want) f |= F_WANT;
-            else { f |= F_PLAINS; s.gs[b] = (int8_t)binade_d(Pa); }
+            if (want && !UNIFORM(b)) f |= F_WANT;
+            else { f |= F_PLAINS; s.gs[b] = (int8_t)binade_d(Pa > 0.0 ? Pa : 1.0); }
         }
         s.flag[b] = f;
     }
@@ -1335,8 +1358,8 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p) {
                 bmax = b > bmax ? b : bmax;
                 const bool crossing = !(ca > 0) || binade_d(ca * (1 - D)) != binade_d(cb * (1 + D));
                 const bool cut = cb >= pp - D && ca <= pp + D;
-                if (crossing || cut || b == from) f |= F_WANT;
-                else { f |= F_PLAINC; s.gc[b] = (int8_t)binade_d(ca); }
+                if ((crossing || cut || b == from) && !UNIFORM(b)) f |= F_WANT;
+                else { f |= F_PLAINC; s.gc[b] = (int8_t)binade_d(ca > 0 ? ca : 1.0); }
             }
         }
         s.flag[b] = f;
@@ -1372,7 +1395,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
     const int lane = threadIdx.x & 31;
 
     // F1: counts and approximate t sums per bin; the tail bin in registers
-    for (int b = threadIdx.x; b < NB; b += NT) { s.cnt[b] = 0; s.tsum32[b] = 0u; }
+    for (int b = threadIdx.x; b < NB; b += NT) { s.cnt[b] = 0; s.tsum32[b] = 0u; s.vmin[b] = 0xffffffffu; s.vmax[b] = 0u; }
     __syncthreads();
     int ninf = 0, ntail = 0;
     for (int i = threadIdx.x; i < r.len; i += NT) {
@@ -1383,6 +1406,9 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
         if (b == NB - 1) { ++ntail; continue; }
         atomicAdd(&s.cnt[b], 1u);
         atomicAdd(&s.tsum32[b], tsum_fixed(x, b));
+        const uint32_t key = qs_key(v);
+        atomicMin(&s.vmin[b], key);
+        atomicMax(&s.vmax[b], key);
     }
     for (int o = 16; o > 0; o >>= 1) ntail += __shfl_down_sync(FULLMASK, ntail, o);
     if (lane == 0 && ntail) atomicAdd(&s.cnt[NB - 1], (uint32_t)ntail);
@@ -1415,6 +1441,9 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
             int8_t g = 0;
             if (b < NB - 1 && s.cnt[b] > 0) {
                 const double Pa = s.pref[b], Pb = s.pref[b] + (double)s.tsum[b];
+                // elements needed for the exact sums: the first bin, predicted
+                // binade crossings, the top-p cut (none for a uniform bin: its
+                // run is added in closed form) ...
                 bool want = (b == 0) || !(Pa > 0.0);
                 if (!want) {
                     g = (int8_t)binade_d(Pa);
@@ -1425,6 +1454,8 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     if (cb >= pp - D && ca <= pp + D) want = true;
                     if (ca > 0 && ca <= pp + D && binade_d(ca * (1 - D)) != binade_d(cb * (1 + D))) want = true;
                 }
+                if (UNIFORM(b)) want = false;
+                // ... and ids: the predicted draw and the top list
                 const double tgt = u * pp;
                 if (cb >= tgt - D && ca <= tgt + D) want = true;
                 if ((long long)cpre[b] < topn) want = true;
@@ -1566,7 +1597,19 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         int b = w.swb;
                         while (true) {
                             b = warp_walk_bins(S, b, NB - 1, s, s.gs, F_PLAINS, POS_INF, true);
-                            if (b >= NB - 1 || !(s.flag[b] & F_GATH)) break;
+                            if (b >= NB - 1) break;
+                            if (UNIFORM(b)) {
+                                // a run of equal terms: closed form
+                                if (threadIdx.x == 0) {
+                                    s.sstart[b] = S;
+                                    const float t = qs_expf(__fsub_rn(qs_unkey(s.vmin[b]), M));
+                                    qs_run_add(&S, t, (long long)s.cnt[b], POS_INF);
+                                }
+                                S = __shfl_sync(FULLMASK, S, 0);
+                                ++b;
+                                continue;
+                            }
+                            if (!(s.flag[b] & F_GATH)) break;
                             const uint32_t off = s.specoff[b];
                             if (threadIdx.x == 0) s.sstart[b] = S;
                             warp_walk_terms(S, (int)s.cnt[b], POS_INF, [&](int i) { return s.spect[off + i]; });
@@ -1620,9 +1663,22 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         int found = -1;
                         while (true) {
                             b = warp_walk_bins(C, b, NB - 1, s, s.gc, F_PLAINC, p.top_p, false);
-                            if (b >= NB - 1 || !(s.flag[b] & F_GATH)) break;
-                            const uint32_t off = s.specoff[b];
+                            if (b >= NB - 1) break;
                             const int n = (int)s.cnt[b];
+                            if (UNIFORM(b)) {
+                                int idx = n;
+                                if (threadIdx.x == 0) {
+                                    const float t = qs_expf(__fsub_rn(qs_unkey(s.vmin[b]), M));
+                                    idx = (int)qs_run_add(&C, __fdiv_rn(t, Sn), (long long)n, p.top_p);
+                                }
+                                C = __shfl_sync(FULLMASK, C, 0);
+                                idx = __shfl_sync(FULLMASK, idx, 0);
+                                if (idx < n) { found = idx; break; }
+                                ++b;
+                                continue;
+                            }
+                            if (!(s.flag[b] & F_GATH)) break;
+                            const uint32_t off = s.specoff[b];
                             const int idx = warp_walk_terms(C, n, p.top_p, [&](int i) { return __fdiv_rn(s.spect[off + i], Sn); });
                             if (idx < n) { found = idx; break; }
                             ++b;
@@ -1631,10 +1687,27 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                             // S at the cutoff: the S walk's state at the bin start plus the bin's prefix
                             float S = s.sstart[b];
                             const uint32_t off = s.specoff[b];
-                            warp_walk_terms(S, found + 1, POS_INF, [&](int i) { return s.spect[off + i]; });
+                            const bool uni = UNIFORM(b);
+                            const float tu = uni ? qs_expf(__fsub_rn(qs_unkey(s.vmin[b]), M)) : 0.0f;
+                            if (uni) {
+                                if (threadIdx.x == 0) qs_run_add(&S, tu, (long long)found + 1, POS_INF);
+                                S = __shfl_sync(FULLMASK, S, 0);
+                            } else {
+                                warp_walk_terms(S, found + 1, POS_INF, [&](int i) { return s.spect[off + i]; });
+                            }
                             if (threadIdx.x == 0) {
                                 double mc = 0.0;
-                                for (int i = 0; i <= found; ++i) mc += (double)__fdiv_rn(s.spect[off + i], S);
+                                if (uni) {
+                                    // survivors of the bin share one probability (the draw
+                                    // tolerates the rounding of a product for long runs)
+                                    const double q = (double)__fdiv_rn(tu, S);
+                                    if (found < 4096)
+                                        for (int i = 0; i <= found; ++i) mc += q;
+                                    else
+                                        mc = q * (double)(found + 1);
+                                } else {
+                                    for (int i = 0; i <= found; ++i) mc += (double)__fdiv_rn(s.spect[off + i], S);
+                                }
                                 w.cut_bin = b;
                                 w.cut_idx = found;
                                 w.Sc = S;
@@ -1713,7 +1786,9 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         w.tgt = tgt;
                         w.draw_rank = cpre[dbin];
                         const bool in_cut = !w.cut_all && dbin == bc;
-                        w.big = (!in_cut && c >= 2 && (int)s.cnt[dbin] > SPEC_CAP / 2) ? 1 : 0;
+                        // a large draw bin is searched in place (weighted select): outside
+                        // the cut bin, or a uniform cut bin (its survivors are its lowest ids)
+                        w.big = (c >= 2 && (int)s.cnt[dbin] > SPEC_CAP / 2 && (!in_cut || UNIFORM(dbin))) ? 1 : 0;
                         int need = -1;
                         if (!w.big) {
                             s.flag[dbin] |= F_WANT;
@@ -1742,8 +1817,10 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                             int id;
                             long long before;
                             float pr;
+                            const bool in_cut = !w.cut_all && w.dbin == bc;
                             leader_weighted_select(cl, s, a.n_s, r.V, w.dbin, (w.tgt - w.acc) * (double)w.Sc, M, w.Sc,
-                                                   id, before, pr);
+                                                   in_cut ? (long long)w.cut_idx : (long long)s.cnt[w.dbin] - 1, id,
+                                                   before, pr);
                             if (threadIdx.x == 0) {
                                 w.draw_id = id;
                                 w.draw_rank += before;

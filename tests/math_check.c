@@ -4,6 +4,7 @@
  *   math_check expf  <part> <nparts>   qs_expf == glibc expf, x in [-104, -0]
  *   math_check tanh  <part> <nparts>   qs_tanhf == (float)tanhl, x >= +0
  *   math_check tanhx <part> <nparts>   list tanh mismatches as "bits result"
+ *   math_check runadd <seed> <cases>    qs_run_add == the sequential float loop
  *
  * Prints "bad=<n>" and exits 0; the driver compares the count.
  */
@@ -35,6 +36,48 @@ int main(int argc, char** argv) {
         }
         /* -inf and the underflow edge */
         if (qs_expf(-INFINITY) != 0.0f) ++bad;
+    } else if (!strcmp(what, "runadd")) {
+        /* random runs: S over many binades (mantissas near the binade edge
+           too), terms from far below half an ulp up to S, exact ties
+           (n + 1/2 ulp), counts up to 30000, random or infinite stops */
+        uint64_t st = 0x9E3779B97F4A7C15ull * (part + 1);
+#define RNG() (st ^= st << 13, st ^= st >> 7, st ^= st << 17, st)
+        for (uint64_t cs = 0; cs < nparts; ++cs) {
+            const int e = (int)(RNG() % 40) - 20;
+            uint32_t mant = (uint32_t)(RNG() & 0x7fffffu);
+            if (RNG() % 4 == 0) mant = 0x7fffffu - (uint32_t)(RNG() % 64);
+            float S0;
+            uint32_t sbits = ((uint32_t)(e + 127) << 23) | mant;
+            memcpy(&S0, &sbits, 4);
+            float t;
+            const int kind = (int)(RNG() % 4);
+            if (kind == 0) { /* an exact tie: (n + 1/2) ulp(S0) */
+                const double ulp = ldexp(1.0, e - 23);
+                const double n = (double)(RNG() % 4096);
+                t = (float)((n + 0.5) * ulp);
+            } else if (kind == 1) { /* a tie at half an ulp of a later binade */
+                const double ulp = ldexp(1.0, e - 22 + (int)(RNG() % 3));
+                t = (float)((double)(RNG() % 64) * ulp + 0.5 * ulp);
+            } else {
+                const double f = ldexp((double)(RNG() % 1000000 + 1) / 1e6, -(int)(RNG() % 40));
+                t = (float)(S0 * f);
+            }
+            const long long c = (long long)(RNG() % 30000) + 1;
+            float stop = INFINITY;
+            if (RNG() % 2) stop = (float)(S0 * (1.0 + (double)(RNG() % 1000) / 100.0));
+            float Sa = S0, Sb = S0;
+            long long ia = c;
+            for (long long q = 0; q < c; ++q) {
+                Sa = Sa + t;
+                if (Sa >= stop) { ia = q; break; }
+            }
+            const long long ib = qs_run_add(&Sb, t, c, stop);
+            if (ia != ib || memcmp(&Sa, &Sb, 4)) {
+                if (bad < 5) printf("mismatch S0=%a t=%a c=%lld stop=%a: loop (%lld, %a) run (%lld, %a)\n", S0, t, c, stop, ia, Sa, ib, Sb);
+                ++bad;
+            }
+        }
+#undef RNG
     } else if (!strcmp(what, "tanh") || !strcmp(what, "tanhx")) {
         const int list = !strcmp(what, "tanhx");
         const uint64_t lo = 0, hi = 0x7F800000u; /* +0 .. +inf */

@@ -45,3 +45,15 @@ def test_expf_matches_glibc_on_whole_domain(checker):
 
 def test_tanhf_correctly_rounded_on_all_floats(checker):
     assert _run_parts(checker, "tanh") == 0
+
+
+def test_run_add_matches_sequential_float_loop(checker):
+    """qs_run_add (a run of equal terms added in O(1) per binade, used by the
+    cluster kernel's walks over bins whose logits are all equal) against the
+    plain loop `S = S + t; if (S >= stop) break;` on random runs, including
+    exact round-half-to-even ties and binade crossings."""
+    procs = [subprocess.Popen([checker, "runadd", str(seed), "20000"], stdout=subprocess.PIPE, text=True)
+             for seed in range(NPARTS)]
+    for p in procs:
+        out, _ = p.communicate()
+        assert p.returncode == 0 and out.strip().endswith("bad=0"), out
