@@ -86,7 +86,7 @@ struct Sm {
     uint32_t* tie;
     uint32_t* vmin;            // per bin: smallest / largest qs_key(value) (uniform bins: equal)
     uint32_t* vmax;
-    int32_t* hist;
+    uint32_t* vcnt;            // elements equal to vmax (low 16 bits) / to vmin (high 16 bits)
     unsigned long long* spec;
     float* spect;
     Misc* misc;
@@ -96,6 +96,40 @@ __device__ __forceinline__ bool uniform_bin(const uint32_t* cnt, const uint32_t*
     return b < NB - 1 && cnt[b] > 0 && vmin[b] == vmax[b];
 }
 #define UNIFORM(b) uniform_bin(s.cnt, s.vmin, s.vmax, (b))
+// A bin whose elements hold exactly two values: two runs of equal terms.
+__device__ __forceinline__ bool twoval_bin(const uint32_t* cnt, const uint32_t* vmin, const uint32_t* vmax,
+                                           const uint32_t* vcnt, int b) {
+    if (b >= NB - 1 || cnt[b] == 0 || vmin[b] == vmax[b]) return false;
+    const uint32_t a = vcnt[b] & 0xffffu, c = vcnt[b] >> 16;
+    return a < 0xffffu && c < 0xffffu && a + c == cnt[b];
+}
+#define RUNBIN(b) (UNIFORM(b) || twoval_bin(s.cnt, s.vmin, s.vmax, s.vcnt, (b)))
+
+// The runs of a uniform or two-valued bin in sorted order: its largest value
+// first. t = qs_expf(value - M).
+struct BinRuns {
+    int n;
+    float t[2];
+    long long c[2];
+};
+__device__ __forceinline__ BinRuns bin_runs(const uint32_t* cnt, const uint32_t* vmin, const uint32_t* vmax,
+                                            const uint32_t* vcnt, int b, float M) {
+    BinRuns R;
+    R.t[0] = qs_expf(__fsub_rn(qs_unkey(vmax[b]), M));
+    if (vmin[b] == vmax[b]) {
+        R.n = 1;
+        R.c[0] = cnt[b];
+        R.t[1] = 0.0f;
+        R.c[1] = 0;
+    } else {
+        R.n = 2;
+        R.c[0] = vcnt[b] & 0xffffu;
+        R.t[1] = qs_expf(__fsub_rn(qs_unkey(vmin[b]), M));
+        R.c[1] = vcnt[b] >> 16;
+    }
+    return R;
+}
+#define BIN_RUNS(b) bin_runs(s.cnt, s.vmin, s.vmax, s.vcnt, (b), M)
 
 __device__ __forceinline__ Sm carve(unsigned char* base, int n_s) {
     const SmemLayout L = smem_layout(n_s);
@@ -118,7 +152,7 @@ __device__ __forceinline__ Sm carve(unsigned char* base, int n_s) {
     s.tie = (uint32_t*)(base + L.off_tie);
     s.vmin = (uint32_t*)(base + L.off_vmin);
     s.vmax = (uint32_t*)(base + L.off_vmax);
-    s.hist = (int32_t*)(base + L.off_hist);
+    s.vcnt = (uint32_t*)(base + L.off_vcnt);
     s.spec = (unsigned long long*)(base + L.off_spec);
     s.spect = (float*)(base + L.off_spect);
     s.misc = (Misc*)(base + L.off_misc);
@@ -569,8 +603,9 @@ __device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s)
 // Penalties over the window (sampling.cpp:124-135 plus the frequency /
 // presence extension): every CTA sorts the window ids, and the leader of
 // each run that falls in this slice recomputes its value.
-constexpr int PF_SLOTS = 2048;  // penalty hash slots: 2 x 2048 ints fit the HIST_MAX window area
-static_assert(2 * PF_SLOTS <= HIST_MAX, "penalty hash table exceeds the window area");
+constexpr int PF_SLOTS = 2048;  // penalty hash slots (ids + counts)
+static_assert(2 * PF_SLOTS * 4 <= SPEC_CAP * 8 && HIST_MAX * 4 <= SPEC_CAP * 8,
+              "the penalty window scratch must fit the gather list");
 
 __device__ void penalty_fixup(const RowCtx& r, const QsLaunch& a, const Sm& s) {
     const qsamp_row_params& p = *r.p;
@@ -588,13 +623,14 @@ __device__ void penalty_fixup(const RowCtx& r, const QsLaunch& a, const Sm& s) {
     // hash table (PF_SLOTS ids + counts in the window area) for windows of
     // up to 1024 ids, a sort for longer ones
     const bool sorted = w > 1024;
-    int32_t* ht_id = s.hist;
-    int32_t* ht_cnt = s.hist + PF_SLOTS;
+    int32_t* win = (int32_t*)s.spec;  // the gather list is free before the row's passes
+    int32_t* ht_id = win;
+    int32_t* ht_cnt = win + PF_SLOTS;
     if (sorted) {
         const int P2 = next_pow2(w);
-        for (int j = threadIdx.x; j < P2; j += NT) s.hist[j] = j < w ? h[j] : 0x7fffffff;
+        for (int j = threadIdx.x; j < P2; j += NT) win[j] = j < w ? h[j] : 0x7fffffff;
         __syncthreads();
-        bitonic_asc_i32(s.hist, P2);
+        bitonic_asc_i32(win, P2);
     } else {
         for (int q = threadIdx.x; q < PF_SLOTS; q += NT) { ht_id[q] = -1; ht_cnt[q] = 0; }
         __syncthreads();
@@ -615,13 +651,13 @@ __device__ void penalty_fixup(const RowCtx& r, const QsLaunch& a, const Sm& s) {
     }
     const int nslots = sorted ? w : PF_SLOTS;
     for (int j = threadIdx.x; j < nslots; j += NT) {
-        const int32_t id = sorted ? s.hist[j] : ht_id[j];
+        const int32_t id = sorted ? win[j] : ht_id[j];
         if (id < r.lo || id >= r.hi) continue;
         int c = 0;
         if (sorted) {
-            if (j > 0 && s.hist[j - 1] == id) continue;
+            if (j > 0 && win[j - 1] == id) continue;
             c = 1;
-            while (j + c < w && s.hist[j + c] == id) ++c;
+            while (j + c < w && win[j + c] == id) ++c;
         } else {
             c = ht_cnt[j];
         }
@@ -1267,8 +1303,11 @@ __device__ void leader_weighted_select(cg::cluster_group& cl, const Sm& s, int n
 // Cluster-wide totals of the per-CTA bin accumulators, written into CTA 0:
 // CTA r sums bins [r*NB/CL, (r+1)*NB/CL) over every CTA, so no CTA reads
 // more than its share. Followed by a cluster barrier.
+// cnt_tsum: counts, approximate sums and value ranges (after F1); vcounts:
+// also the counts at the range ends (bf16 rows); ks: k-sums of bins
+// [kfrom, kto]; tx: exact t sums.
 __device__ void cluster_reduce_bins(cg::cluster_group& cl, const Sm& s, bool cnt_tsum, bool ks, int kfrom, int kto,
-                                    bool tx) {
+                                    bool tx, bool vcounts = false) {
     const int rank = cl.block_rank(), CL = cl.num_blocks();
     const int per = NB / CL;
     const int b0 = rank * per;
@@ -1283,9 +1322,18 @@ __device__ void cluster_reduce_bins(cg::cluster_group& cl, const Sm& s, bool cnt
                 lo = a0 < lo ? a0 : lo;
                 hi = a1 > hi ? a1 : hi;
             }
+            // elements equal to the bin's largest / smallest value, from the
+            // CTAs whose own extreme is that value (saturating at 0xffff)
+            uint32_t cmax = 0, cmin = 0;
+            for (int q = 0; q < CL && vcounts; ++q) {
+                const uint32_t a0 = peer(cl, s.vmin, q)[b], a1 = peer(cl, s.vmax, q)[b], vc = peer(cl, s.vcnt, q)[b];
+                if (a1 == hi) cmax += vc & 0xffffu;
+                if (a0 == lo) cmin += a0 == a1 ? (vc & 0xffffu) : (vc >> 16);
+            }
             peer(cl, s.cnt, 0)[b] = c;
             peer(cl, s.vmin, 0)[b] = lo;
             peer(cl, s.vmax, 0)[b] = hi;
+            peer(cl, s.vcnt, 0)[b] = (cmax < 0xffffu ? cmax : 0xffffu) | ((cmin < 0xffffu ? cmin : 0xffffu) << 16);
             peer(cl, s.tsum, 0)[b] = b < NB - 1 ? (float)((double)t * (double)tsum_scale(b)) : 0.0f;
         }
         if (ks && b >= kfrom && b <= kto) {
@@ -1327,7 +1375,7 @@ __device__ void predict_s(const Sm& s, int from, double ratio) {
         if (b >= from && b < NB - 1 && s.cnt[b] > 0) {
             const double Pa = s.pref[b] * ratio, Pb = (s.pref[b] + (double)TX(b) * 0x1p-40) * ratio;
             const bool want = b == from || !(Pa > 0.0) || binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
-            if (want && !UNIFORM(b)) f |= F_WANT;
+            if (want && !RUNBIN(b)) f |= F_WANT;
             else { f |= F_PLAINS; s.gs[b] = (int8_t)binade_d(Pa > 0.0 ? Pa : 1.0); }
         }
         s.flag[b] = f;
@@ -1358,7 +1406,7 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p) {
                 bmax = b > bmax ? b : bmax;
                 const bool crossing = !(ca > 0) || binade_d(ca * (1 - D)) != binade_d(cb * (1 + D));
                 const bool cut = cb >= pp - D && ca <= pp + D;
-                if ((crossing || cut || b == from) && !UNIFORM(b)) f |= F_WANT;
+                if ((crossing || cut || b == from) && !RUNBIN(b)) f |= F_WANT;
                 else { f |= F_PLAINC; s.gc[b] = (int8_t)binade_d(ca > 0 ? ca : 1.0); }
             }
         }
@@ -1395,7 +1443,13 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
     const int lane = threadIdx.x & 31;
 
     // F1: counts and approximate t sums per bin; the tail bin in registers
-    for (int b = threadIdx.x; b < NB; b += NT) { s.cnt[b] = 0; s.tsum32[b] = 0u; s.vmin[b] = 0xffffffffu; s.vmax[b] = 0u; }
+    for (int b = threadIdx.x; b < NB; b += NT) {
+        s.cnt[b] = 0;
+        s.tsum32[b] = 0u;
+        s.vmin[b] = 0xffffffffu;
+        s.vmax[b] = 0u;
+        s.vcnt[b] = 0u;
+    }
     __syncthreads();
     int ninf = 0, ntail = 0;
     for (int i = threadIdx.x; i < r.len; i += NT) {
@@ -1412,12 +1466,24 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
     }
     for (int o = 16; o > 0; o >>= 1) ntail += __shfl_down_sync(FULLMASK, ntail, o);
     if (lane == 0 && ntail) atomicAdd(&s.cnt[NB - 1], (uint32_t)ntail);
-    ninf = block_sum_int(ninf, m);
+    ninf = block_sum_int(ninf, m);  // (its barriers also complete the min / max updates)
+    // per bin, this CTA's elements equal to its largest / smallest value: only
+    // for bf16 rows, where equal logits fill whole bins (without the counts a
+    // two-valued bin is gathered like any other)
+    for (int i = threadIdx.x; r.dtype == QSAMP_BF16 && i < r.len; i += NT) {
+        const float v = s.vals[i];
+        if (v == NEG_INF) continue;
+        const int b = binof(__fsub_rn(v, M));
+        if (b == NB - 1) continue;
+        const uint32_t key = qs_key(v);
+        if (key == s.vmax[b]) atomicAdd(&s.vcnt[b], 1u);
+        else if (key == s.vmin[b]) atomicAdd(&s.vcnt[b], 0x10000u);
+    }
     if (threadIdx.x == 0) { m->ninf = ninf; m->neg_quota = 0; }
     __syncthreads();
     QS_TMARK(r.row, 5, rank == 0);
     cl.sync();
-    cluster_reduce_bins(cl, s, true, false, 0, -1, false);
+    cluster_reduce_bins(cl, s, true, false, 0, -1, false, r.dtype == QSAMP_BF16);
     QS_TMARK(r.row, 6, rank == 0);
 
     if (rank == 0) {
@@ -1454,7 +1520,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     if (cb >= pp - D && ca <= pp + D) want = true;
                     if (ca > 0 && ca <= pp + D && binade_d(ca * (1 - D)) != binade_d(cb * (1 + D))) want = true;
                 }
-                if (UNIFORM(b)) want = false;
+                if (RUNBIN(b)) want = false;
                 // ... and ids: the predicted draw and the top list
                 const double tgt = u * pp;
                 if (cb >= tgt - D && ca <= tgt + D) want = true;
@@ -1598,12 +1664,15 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         while (true) {
                             b = warp_walk_bins(S, b, NB - 1, s, s.gs, F_PLAINS, POS_INF, true);
                             if (b >= NB - 1) break;
-                            if (UNIFORM(b)) {
-                                // a run of equal terms: closed form
+                            if (RUNBIN(b)) {
+                                // one or two runs of equal terms: closed form
                                 if (threadIdx.x == 0) {
                                     s.sstart[b] = S;
-                                    const float t = qs_expf(__fsub_rn(qs_unkey(s.vmin[b]), M));
-                                    qs_run_add(&S, t, (long long)s.cnt[b], POS_INF);
+                                    const BinRuns R = BIN_RUNS(b);
+                                    
+#pragma unroll
+                                    for (int q = 0; q < 2; ++q)
+                                        if (q < R.n) qs_run_add(&S, R.t[q], R.c[q], POS_INF);
                                 }
                                 S = __shfl_sync(FULLMASK, S, 0);
                                 ++b;
@@ -1665,11 +1734,18 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                             b = warp_walk_bins(C, b, NB - 1, s, s.gc, F_PLAINC, p.top_p, false);
                             if (b >= NB - 1) break;
                             const int n = (int)s.cnt[b];
-                            if (UNIFORM(b)) {
+                            if (RUNBIN(b)) {
                                 int idx = n;
                                 if (threadIdx.x == 0) {
-                                    const float t = qs_expf(__fsub_rn(qs_unkey(s.vmin[b]), M));
-                                    idx = (int)qs_run_add(&C, __fdiv_rn(t, Sn), (long long)n, p.top_p);
+                                    const BinRuns R = BIN_RUNS(b);
+                                    long long before = 0;
+#pragma unroll
+                                    for (int q = 0; q < 2; ++q) {
+                                        if (q >= R.n || idx < n) continue;
+                                        const long long j = qs_run_add(&C, __fdiv_rn(R.t[q], Sn), R.c[q], p.top_p);
+                                        if (j < R.c[q]) { idx = (int)(before + j); continue; }
+                                        before += R.c[q];
+                                    }
                                 }
                                 C = __shfl_sync(FULLMASK, C, 0);
                                 idx = __shfl_sync(FULLMASK, idx, 0);
@@ -1687,24 +1763,43 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                             // S at the cutoff: the S walk's state at the bin start plus the bin's prefix
                             float S = s.sstart[b];
                             const uint32_t off = s.specoff[b];
-                            const bool uni = UNIFORM(b);
-                            const float tu = uni ? qs_expf(__fsub_rn(qs_unkey(s.vmin[b]), M)) : 0.0f;
-                            if (uni) {
-                                if (threadIdx.x == 0) qs_run_add(&S, tu, (long long)found + 1, POS_INF);
+                            const bool runs = RUNBIN(b);
+                            if (runs) {
+                                if (threadIdx.x == 0) {
+                                    const BinRuns R = BIN_RUNS(b);
+                                    long long left = (long long)found + 1;
+                                    
+#pragma unroll
+                                    for (int q = 0; q < 2; ++q) {
+                                        if (q >= R.n || left <= 0) continue;
+                                        const long long take = left < R.c[q] ? left : R.c[q];
+                                        qs_run_add(&S, R.t[q], take, POS_INF);
+                                        left -= take;
+                                    }
+                                }
                                 S = __shfl_sync(FULLMASK, S, 0);
                             } else {
                                 warp_walk_terms(S, found + 1, POS_INF, [&](int i) { return s.spect[off + i]; });
                             }
                             if (threadIdx.x == 0) {
                                 double mc = 0.0;
-                                if (uni) {
-                                    // survivors of the bin share one probability (the draw
+                                if (runs) {
+                                    // survivors of one run share one probability (the draw
                                     // tolerates the rounding of a product for long runs)
-                                    const double q = (double)__fdiv_rn(tu, S);
-                                    if (found < 4096)
-                                        for (int i = 0; i <= found; ++i) mc += q;
-                                    else
-                                        mc = q * (double)(found + 1);
+                                    const BinRuns R = BIN_RUNS(b);
+                                    long long left = (long long)found + 1;
+                                    
+#pragma unroll
+                                    for (int q = 0; q < 2; ++q) {
+                                        if (q >= R.n || left <= 0) continue;
+                                        const long long take = left < R.c[q] ? left : R.c[q];
+                                        const double pq = (double)__fdiv_rn(R.t[q], S);
+                                        if (take < 4096)
+                                            for (long long i = 0; i < take; ++i) mc += pq;
+                                        else
+                                            mc += pq * (double)take;
+                                        left -= take;
+                                    }
                                 } else {
                                     for (int i = 0; i <= found; ++i) mc += (double)__fdiv_rn(s.spect[off + i], S);
                                 }
@@ -1788,7 +1883,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         const bool in_cut = !w.cut_all && dbin == bc;
                         // a large draw bin is searched in place (weighted select): outside
                         // the cut bin, or a uniform cut bin (its survivors are its lowest ids)
-                        w.big = (c >= 2 && (int)s.cnt[dbin] > SPEC_CAP / 2 && (!in_cut || UNIFORM(dbin))) ? 1 : 0;
+                        w.big = (c >= 2 && (int)s.cnt[dbin] > SPEC_CAP / 2 && (!in_cut || RUNBIN(dbin))) ? 1 : 0;
                         int need = -1;
                         if (!w.big) {
                             s.flag[dbin] |= F_WANT;
