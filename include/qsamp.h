@@ -161,6 +161,28 @@ qsamp_status qsamp_keep_list_mask(const char* path, int32_t V, uint32_t* mask_ou
 /* AND two allow-masks word by word (pruning AND grammar). */
 qsamp_status qsamp_mask_and(const uint32_t* a, const uint32_t* b, int64_t words, uint32_t* out);
 
+/* Grammar char classes on the device. ------------------------------------
+ * TokenTrie::mark_char_class (token-trie.cpp:93-116) marks every token whose
+ * FIRST byte the class allows (empty tokens are never marked, token-trie.cpp
+ * :18); GrammarVocab::get_valid_tokens calls it once per distinct char class
+ * among the grammar's stacks (grammar_vocab.cpp:589-597), ~150K ids for a
+ * negated class such as [^"]. Here the marks of B grammar states are made at
+ * once on the GPU, straight into the allow-masks qsamp_sample reads.
+ *
+ * qsamp_first_byte_table (host): table[i] = first byte of token i (0..255),
+ * 256 for an empty token; copy it to the device once per vocabulary.
+ * qsamp_char_class_masks: for row b, bit i of masks[b] is set when token i's
+ * first byte is allowed by classes[b] (256 bits, bit c%32 of word c/32, with a
+ * negated class already complemented); or_into = 1 ORs into the existing
+ * words (a state with several char classes, or literal ids packed before),
+ * 0 overwrites them. table, classes [B][8] and masks [B][mask_stride] are
+ * DEVICE pointers; stream-ordered. No counterpart of the batching in the
+ * reference (its marks are per state, on the host). */
+qsamp_status qsamp_first_byte_table(const char* const* strs, const int32_t* lens, int32_t V, uint16_t* table_out);
+qsamp_status qsamp_char_class_masks(qsamp_ctx* ctx, const uint16_t* table, int32_t V, int32_t B,
+                                    const uint32_t* classes, uint32_t* masks, int64_t mask_stride, int32_t or_into,
+                                    void* stream);
+
 /* Vocab-sharded selection (tensor-parallel output head). No counterpart in
  * the reference (its sampler sees whole rows). ----------------------------
  * Rank r holds logits[:, v_offset : v_offset + V_local] of a V_total vocab

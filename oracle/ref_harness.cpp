@@ -24,6 +24,7 @@
 #include "ref_access.h"
 
 #include <atomic>
+#include <set>
 #include <cstdint>
 #include <cstring>
 #include <random>
@@ -120,6 +121,17 @@ int qwref_grammar_accepting(void* g) {
     return static_cast<qwenium::GrammarVocab*>(g)->is_accepting_state() ? 1 : 0;
 }
 void qwref_grammar_reset(void* g) { static_cast<qwenium::GrammarVocab*>(g)->reset(); }
+
+// TokenTrie::mark_char_class (token-trie.cpp:93-116) into a fresh mask:
+// out[i] = 1 when the reference marks token i.
+void qwref_trie_mark_char_class(void* trie, const unsigned char* chars, int n, int negated, int V,
+                                unsigned char* out) {
+    std::set<char> cs;
+    for (int i = 0; i < n; ++i) cs.insert(static_cast<char>(chars[i]));
+    std::vector<bool> mask(static_cast<size_t>(V), false);
+    static_cast<qwenium::TokenTrie*>(trie)->mark_char_class(cs, negated != 0, mask);
+    for (int i = 0; i < V; ++i) out[i] = mask[static_cast<size_t>(i)] ? 1 : 0;
+}
 
 // The full Sampler::sample path with a grammar, an EOS id and/or a pruning
 // keep-set attached (sampling.cpp:12-81): exercises apply_vocab_pruning,

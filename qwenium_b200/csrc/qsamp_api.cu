@@ -24,6 +24,9 @@ extern "C" cudaError_t qs_stream_attrs(size_t smem);
 extern "C" cudaError_t qs_stream_occupancy(size_t smem, int* blocks_per_sm);
 extern "C" cudaError_t qs_launch_stream(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st);
 extern "C" size_t qs_merge_smem();
+extern "C" cudaError_t qs_launch_char_class(const uint16_t* table, int V, int B, const uint32_t* classes,
+                                            uint32_t* masks, long long mask_stride, int or_into, int num_sms,
+                                            cudaStream_t st);
 extern "C" cudaError_t qs_merge_attrs(size_t smem);
 extern "C" cudaError_t qs_launch_merge(const qs::QsLaunch* a, const float* all_vals, const int32_t* all_ids,
                                        int n_ranks, int kc, int grid, size_t smem, cudaStream_t st);
@@ -773,6 +776,36 @@ qsamp_status qsamp_mask_and(const uint32_t* a, const uint32_t* b, int64_t words,
     if (!a || !b || !out || words < 0) return QSAMP_ERR_INVALID_ARG;
     for (int64_t i = 0; i < words; ++i) out[i] = a[i] & b[i];
     return QSAMP_OK;
+}
+
+qsamp_status qsamp_first_byte_table(const char* const* strs, const int32_t* lens, int32_t V, uint16_t* table_out) {
+    if (V < 1 || !strs || !lens || !table_out) return QSAMP_ERR_INVALID_ARG;
+    for (int32_t i = 0; i < V; ++i)
+        table_out[i] = (lens[i] > 0 && strs[i]) ? (uint16_t)(unsigned char)strs[i][0] : (uint16_t)256;
+    return QSAMP_OK;
+}
+
+qsamp_status qsamp_char_class_masks(qsamp_ctx* c, const uint16_t* table, int32_t V, int32_t B,
+                                    const uint32_t* classes, uint32_t* masks, int64_t mask_stride, int32_t or_into,
+                                    void* stream) {
+    if (!c) return QSAMP_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (V < 1) return fail(c, QSAMP_ERR_INVALID_ARG, "V: expected >= 1, got %d", V);
+    if (B < 0 || B > 65535) return fail(c, QSAMP_ERR_INVALID_ARG, "B: expected [0,65535], got %d", B);
+    if (B == 0) return QSAMP_OK;
+    if (!table || !classes || !masks) return fail(c, QSAMP_ERR_INVALID_ARG, "table/classes/masks: expected non-NULL");
+    const long long words = (V + 31) / 32;
+    if (mask_stride < words)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "mask_stride: expected >= %lld words, got %lld", words,
+                    (long long)mask_stride);
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != c->device) cudaSetDevice(c->device);
+    cudaError_t e = qs_launch_char_class(table, V, B, classes, masks, mask_stride, or_into ? 1 : 0, c->num_sms,
+                                         (cudaStream_t)stream);
+    if (e == cudaSuccess) c->ctr.kernel_launches += 1;
+    if (prev != c->device) cudaSetDevice(prev);
+    return e == cudaSuccess ? QSAMP_OK : cuda_fail(c, e, "char-class mask launch");
 }
 
 // ---------------------------------------------------------------- sharded

@@ -2711,6 +2711,57 @@ __global__ void __launch_bounds__(SN_NT, 1) qs_merge_kernel(QsLaunch a, const fl
     }
 }
 
+// ============================================================ char-class masks
+// One thread per 32-bit mask word and CC_ROWS rows: the 32 tokens' first
+// bytes are read once (64 consecutive bytes of the table, coalesced across
+// the warp) and looked up in each row's 256-bit class (shared memory; index
+// 256 = an empty token, never allowed). HBM-bound on the mask writes.
+constexpr int CC_ROWS = 8;
+__global__ void __launch_bounds__(256) qs_char_class_kernel(const uint16_t* table, int V, int B,
+                                                            const uint32_t* classes, uint32_t* masks,
+                                                            long long mask_stride, int or_into, int vec) {
+    const int r0 = blockIdx.y * CC_ROWS;
+    const int nr = min(CC_ROWS, B - r0);
+    __shared__ uint32_t cls[CC_ROWS][9];
+    for (int q = threadIdx.x; q < CC_ROWS * 9; q += blockDim.x) {
+        const int rr = q / 9, w = q % 9;
+        cls[rr][w] = (rr < nr && w < 8) ? classes[(size_t)(r0 + rr) * 8 + w] : 0u;
+    }
+    __syncthreads();
+    const int words = (V + 31) / 32;
+    for (int w = blockIdx.x * blockDim.x + threadIdx.x; w < words; w += gridDim.x * blockDim.x) {
+        const int i0 = w * 32;
+        uint32_t fb[16];  // 32 first bytes, two per word
+        if (vec && i0 + 32 <= V) {
+            const uint4* t4 = (const uint4*)(table + i0);  // 16-byte aligned: i0 is a multiple of 32
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint4 v = __ldg(t4 + q);
+                fb[4 * q] = v.x; fb[4 * q + 1] = v.y; fb[4 * q + 2] = v.z; fb[4 * q + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                const uint32_t lo = i0 + 2 * q < V ? table[i0 + 2 * q] : 256u;
+                const uint32_t hi = i0 + 2 * q + 1 < V ? table[i0 + 2 * q + 1] : 256u;
+                fb[q] = lo | (hi << 16);
+            }
+        }
+        for (int rr = 0; rr < nr; ++rr) {
+            const uint32_t* c = cls[rr];
+            uint32_t bits = 0u;
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                const uint32_t lo = fb[q] & 0xffffu, hi = fb[q] >> 16;
+                bits |= ((c[lo >> 5] >> (lo & 31)) & 1u) << (2 * q);
+                bits |= ((c[hi >> 5] >> (hi & 31)) & 1u) << (2 * q + 1);
+            }
+            uint32_t* out = masks + (size_t)(r0 + rr) * (size_t)mask_stride + w;
+            *out = or_into ? (*out | bits) : bits;
+        }
+    }
+}
+
 }  // namespace qs
 
 // launch helpers used by qsamp_api.cu
@@ -2766,6 +2817,19 @@ extern "C" cudaError_t qs_launch_lut(float* lut, float cap, cudaStream_t st) {
 extern "C" size_t qs_stream_smem(int V) { return (size_t)qs::sn_layout(V).total; }
 
 extern "C" size_t qs_merge_smem() { return (size_t)qs::mg_layout().total; }
+extern "C" cudaError_t qs_launch_char_class(const uint16_t* table, int V, int B, const uint32_t* classes,
+                                            uint32_t* masks, long long mask_stride, int or_into, int num_sms,
+                                            cudaStream_t st) {
+    const int words = (V + 31) / 32;
+    const int gy = (B + qs::CC_ROWS - 1) / qs::CC_ROWS;
+    int gx = (words + 255) / 256;
+    const int cap = (4 * num_sms + gy - 1) / gy;  // about four CTAs per SM over the batch
+    if (gx > cap) gx = cap > 0 ? cap : 1;
+    const int vec = ((uintptr_t)table % 16) == 0;
+    qs::qs_char_class_kernel<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, st>>>(table, V, B, classes, masks,
+                                                                              mask_stride, or_into, vec);
+    return cudaGetLastError();
+}
 extern "C" cudaError_t qs_merge_attrs(size_t smem) {
     return cudaFuncSetAttribute(qs::qs_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }

@@ -63,7 +63,7 @@ EXPORTS = (
     "qsamp_create", "qsamp_destroy", "qsamp_last_error", "qsamp_sample", "qsamp_sample_host",
     "qsamp_pack_ids", "qsamp_grammar_mask", "qsamp_find_eos_string", "qsamp_keep_list_mask",
     "qsamp_mask_and", "qsamp_shard_topk", "qsamp_merge_topk", "qsamp_get_counters", "qsamp_set_kernel_timing",
-    "qsamp_sample_static",
+    "qsamp_sample_static", "qsamp_first_byte_table", "qsamp_char_class_masks",
 )
 
 _P = ctypes.c_void_p
@@ -152,6 +152,11 @@ def load(path: str = LIB_PATH):
                                      ctypes.c_uint64, _P, _P, _P]
     lib.qsamp_get_counters.restype = ctypes.c_int
     lib.qsamp_get_counters.argtypes = [_P, ctypes.POINTER(_Counters)]
+    lib.qsamp_first_byte_table.restype = ctypes.c_int
+    lib.qsamp_first_byte_table.argtypes = [_P, _P, ctypes.c_int32, _P]
+    lib.qsamp_char_class_masks.restype = ctypes.c_int
+    lib.qsamp_char_class_masks.argtypes = [_P, _P, ctypes.c_int32, ctypes.c_int32, _P, _P, ctypes.c_int64,
+                                           ctypes.c_int32, _P]
     lib.qsamp_set_kernel_timing.restype = ctypes.c_int
     lib.qsamp_set_kernel_timing.argtypes = [_P, ctypes.c_int32]
     lib.qsamp_sample_static.restype = ctypes.c_int
@@ -210,6 +215,32 @@ def find_eos_string(strs: Sequence) -> int:
     return lib.qsamp_find_eos_string(ctypes.cast(arr, _P), _np_ptr(lens), len(bs))
 
 
+def first_byte_table(strs: Sequence) -> np.ndarray:
+    """qsamp_first_byte_table: first byte of each token (256: empty token)."""
+    lib = load()
+    bs = [s.encode("latin-1") if isinstance(s, str) else bytes(s) for s in strs]
+    bufs = [ctypes.create_string_buffer(b, len(b) + 1) for b in bs]
+    arr = (ctypes.c_void_p * len(bs))(*[ctypes.addressof(b) for b in bufs])
+    lens = np.array([len(b) for b in bs], np.int32)
+    out = np.empty(len(bs), np.uint16)
+    rc = lib.qsamp_first_byte_table(ctypes.cast(arr, _P), _np_ptr(lens), len(bs), _np_ptr(out))
+    if rc:
+        raise QsampError(rc, "qsamp_first_byte_table")
+    return out
+
+
+def char_class_bits(chars, negated: bool) -> np.ndarray:
+    """The 256-bit allowed set of a grammar char class (8 uint32 words), as
+    TokenTrie::mark_char_class builds its lookup table (token-trie.cpp:96-104):
+    the class's bytes, or their complement for a negated class."""
+    allowed = np.zeros(256, bool)
+    idx = np.array([int(c) if isinstance(c, (int, np.integer)) else ord(c) for c in chars], np.int64) & 0xFF
+    allowed[idx] = True
+    if negated:
+        allowed = ~allowed
+    return np.packbits(allowed, bitorder="little").view(np.uint32).copy()
+
+
 def keep_list_mask(path: str, V: int) -> np.ndarray:
     lib = load()
     out = np.zeros(words_for(V), np.uint32)
@@ -261,6 +292,20 @@ class Context:
     def set_kernel_timing(self, on: bool):
         """Bracket each selection kernel with CUDA events (see counters())."""
         self._check(self.lib.qsamp_set_kernel_timing(self.h, 1 if on else 0), "qsamp_set_kernel_timing")
+
+    def char_class_masks(self, table, classes, masks, or_into: bool = False, stream=None):
+        """qsamp_char_class_masks on CUDA tensors: table uint16 [V] (as int16),
+        classes uint32 [B][8] (as int32), masks uint32 [B][stride] (as int32)."""
+        import torch
+
+        V = int(table.shape[0])
+        B = int(classes.shape[0])
+        if stream is None:
+            stream = torch.cuda.current_stream(masks.device).cuda_stream
+        self._check(self.lib.qsamp_char_class_masks(self.h, _dev_ptr(table), V, B, _dev_ptr(classes), _dev_ptr(masks),
+                                                    int(masks.stride(0)), 1 if or_into else 0,
+                                                    ctypes.c_void_p(stream)), "qsamp_char_class_masks")
+        return masks
 
     def counters(self) -> dict:
         c = _Counters()
