@@ -210,6 +210,24 @@ qsamp_status qsamp_merge_topk(qsamp_ctx* ctx, int32_t n_ranks, int32_t B, int32_
                               const qsamp_row_params* params, const double* u, uint64_t rng_offset,
                               int32_t* out_ids, qsamp_row_result* out_results, void* stream);
 
+/* Greedy verification of prompt-lookup drafts (speculative decoding). -----
+ * SpeculativeDecoder::try_speculative_step (speculative.h:150-239) runs a
+ * slot's K draft tokens through the model in one pass and accepts them
+ * greedily: row i of the K logits rows must predict draft[i+1]
+ * (argmax, speculative.h:248-258: the first maximum, NaN never larger, a NaN
+ * at index 0 wins), an accepted EOS draft stops the step, and the bonus token
+ * is the argmax at the first mismatch or after the last row. Here the rows of
+ * B slots are verified at once on the device. Slot b owns rows
+ * [row_off[b], row_off[b+1]) of logits (DEVICE [n_rows][row_stride], dtype)
+ * and the same entries of drafts; row_off (DEVICE [B+1], row_off[0] = 0,
+ * row_off[B] = n_rows). Outputs (DEVICE [B]): accepted (draft tokens kept),
+ * bonus (or -1), has_bonus (bonus != eos_token). K = 0: 0, -1, 0 (no draft).
+ * No counterpart of the batching in the reference (one slot per call). */
+qsamp_status qsamp_verify_greedy(qsamp_ctx* ctx, const void* logits, qsamp_dtype dtype, int32_t V, int64_t row_stride,
+                                 int32_t n_rows, int32_t B, const int32_t* row_off, const int32_t* drafts,
+                                 int32_t eos_token, int32_t* out_accepted, int32_t* out_bonus,
+                                 int32_t* out_has_bonus, void* stream);
+
 /* Counters since creation (observability). No counterpart in the
  * reference. kernel_launches counts every kernel this context launched
  * (selection, merge, soft-cap tables). With kernel timing on, each selection

@@ -133,6 +133,8 @@ def ref_lib(kind: str = "strict"):
         lib.qwref_grammar_accepting.restype = ctypes.c_int
         lib.qwref_grammar_accepting.argtypes = [_P]
         lib.qwref_grammar_reset.argtypes = [_P]
+        lib.qwref_spec_verify.restype = None
+        lib.qwref_spec_verify.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P, _P]
         lib.qwref_trie_mark_char_class.restype = None
         lib.qwref_trie_mark_char_class.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P]
         lib.qwref_sampler_sample_full.restype = ctypes.c_int

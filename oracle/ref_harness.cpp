@@ -21,6 +21,7 @@
 #include "sampling.h"
 #include "grammar_vocab.h"
 #include "token-trie.h"
+#include "speculative.h"
 #include "ref_access.h"
 
 #include <atomic>
@@ -121,6 +122,32 @@ int qwref_grammar_accepting(void* g) {
     return static_cast<qwenium::GrammarVocab*>(g)->is_accepting_state() ? 1 : 0;
 }
 void qwref_grammar_reset(void* g) { static_cast<qwenium::GrammarVocab*>(g)->reset(); }
+
+// SpeculativeDecoder::try_speculative_step (speculative.h:150-239) with a
+// given draft: the prompt ends with three sentinel ids followed by the draft
+// and the generated tokens end with the same three ids, so the n-gram lookup
+// (prompt_lookup.h:33-80, n = 3, max_draft = K) proposes exactly the draft;
+// the verify callback returns the K given logits rows.
+void qwref_spec_verify(const float* logits, int K, int V, const int32_t* draft, int eos, int32_t* accepted,
+                       int32_t* bonus, int32_t* has_bonus) {
+    const int32_t s0 = -1000001, s1 = -1000002, s2 = -1000003;
+    std::vector<int32_t> prompt = {s0, s1, s2};
+    prompt.insert(prompt.end(), draft, draft + K);
+    const std::vector<int32_t> generated = {s0, s1, s2};
+    qwenium::PromptLookupConfig cfg;
+    cfg.ngram_size = 3;
+    cfg.max_draft = K;
+    cfg.min_draft = 1;
+    qwenium::SpeculativeDecoder dec(cfg, V);
+    auto verify = [&](int, const std::vector<int32_t>&, int) {
+        return std::vector<float>(logits, logits + (size_t)K * (size_t)V);
+    };
+    auto rewind = [](int, int) {};
+    const qwenium::SpeculativeResult r = dec.try_speculative_step(prompt, generated, 0, 0, verify, rewind, eos);
+    *accepted = (int32_t)r.accepted_tokens.size();
+    *bonus = r.bonus_token;
+    *has_bonus = r.has_bonus ? 1 : 0;
+}
 
 // TokenTrie::mark_char_class (token-trie.cpp:93-116) into a fresh mask:
 // out[i] = 1 when the reference marks token i.

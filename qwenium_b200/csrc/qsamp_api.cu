@@ -24,6 +24,10 @@ extern "C" cudaError_t qs_stream_attrs(size_t smem);
 extern "C" cudaError_t qs_stream_occupancy(size_t smem, int* blocks_per_sm);
 extern "C" cudaError_t qs_launch_stream(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st);
 extern "C" size_t qs_merge_smem();
+extern "C" cudaError_t qs_launch_verify(const void* logits, int dtype, int V, long long row_stride, int n_rows, int B,
+                                        const int32_t* row_off, const int32_t* drafts, int eos, int32_t* out_acc,
+                                        int32_t* out_bonus, int32_t* out_has, unsigned long long* parts, int segs,
+                                        cudaStream_t st);
 extern "C" cudaError_t qs_launch_char_class(const uint16_t* table, int V, int B, const uint32_t* classes,
                                             uint32_t* masks, long long mask_stride, int or_into, int num_sms,
                                             cudaStream_t st);
@@ -89,6 +93,7 @@ struct qsamp_ctx {
     cudaStream_t copy = nullptr;
     cudaEvent_t copy_go = nullptr, copy_done = nullptr;
     DevBuf<int> ready;
+    DevBuf<unsigned long long> vparts;  // greedy verification: per-segment argmax keys
     int* pinned_one = nullptr;
     size_t attrs_smem = 0;
     size_t max_dyn = 0;    // largest dynamic shared memory a CTA of the kernel may use
@@ -344,6 +349,7 @@ void qsamp_destroy(qsamp_ctx* c) {
     for (cudaEvent_t ev : c->ev)
         if (ev) cudaEventDestroy(ev);
     c->ready.release();
+    c->vparts.release();
     if (c->pinned_one) cudaFreeHost(c->pinned_one);
     if (c->copy_go) cudaEventDestroy(c->copy_go);
     if (c->copy_done) cudaEventDestroy(c->copy_done);
@@ -776,6 +782,35 @@ qsamp_status qsamp_mask_and(const uint32_t* a, const uint32_t* b, int64_t words,
     if (!a || !b || !out || words < 0) return QSAMP_ERR_INVALID_ARG;
     for (int64_t i = 0; i < words; ++i) out[i] = a[i] & b[i];
     return QSAMP_OK;
+}
+
+qsamp_status qsamp_verify_greedy(qsamp_ctx* c, const void* logits, qsamp_dtype dtype, int32_t V, int64_t row_stride,
+                                 int32_t n_rows, int32_t B, const int32_t* row_off, const int32_t* drafts,
+                                 int32_t eos_token, int32_t* out_accepted, int32_t* out_bonus,
+                                 int32_t* out_has_bonus, void* stream) {
+    if (!c) return QSAMP_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (V < 1) return fail(c, QSAMP_ERR_INVALID_ARG, "V: expected >= 1, got %d", V);
+    if (row_stride < V)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "row_stride: expected >= V (%d), got %lld", V, (long long)row_stride);
+    if (dtype != QSAMP_F32 && dtype != QSAMP_BF16)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "dtype: expected QSAMP_F32 or QSAMP_BF16, got %d", (int)dtype);
+    if (n_rows < 0 || B < 0) return fail(c, QSAMP_ERR_INVALID_ARG, "n_rows / B: expected >= 0, got %d / %d", n_rows, B);
+    if (B == 0) return QSAMP_OK;
+    if (!row_off || !out_accepted || !out_bonus || !out_has_bonus || (n_rows > 0 && (!logits || !drafts)))
+        return fail(c, QSAMP_ERR_INVALID_ARG, "row_off / drafts / logits / outputs: expected non-NULL");
+    int prev = 0;
+    cudaGetDevice(&prev);
+    if (prev != c->device) cudaSetDevice(c->device);
+    int segs = n_rows > 0 ? (2 * c->num_sms + n_rows - 1) / n_rows : 1;
+    segs = segs < 1 ? 1 : (segs > 64 ? 64 : segs);
+    cudaError_t e = c->vparts.ensure((size_t)(n_rows > 0 ? n_rows : 1) * segs);
+    if (e == cudaSuccess)
+        e = qs_launch_verify(logits, (int)dtype, V, row_stride, n_rows, B, row_off, drafts, eos_token, out_accepted,
+                             out_bonus, out_has_bonus, c->vparts.p, segs, (cudaStream_t)stream);
+    if (e == cudaSuccess) c->ctr.kernel_launches += n_rows > 0 ? 2 : 1;
+    if (prev != c->device) cudaSetDevice(prev);
+    return e == cudaSuccess ? QSAMP_OK : cuda_fail(c, e, "greedy verification launch");
 }
 
 qsamp_status qsamp_first_byte_table(const char* const* strs, const int32_t* lens, int32_t V, uint16_t* table_out) {

@@ -2762,6 +2762,118 @@ __global__ void __launch_bounds__(256) qs_char_class_kernel(const uint16_t* tabl
     }
 }
 
+// ============================================================ greedy verification
+// Speculative decoding's argmax (speculative.h:248-258) over K rows of B
+// slots. Stage 1: a row is split over `segs` CTAs; each keeps its segment's
+// best key (ordered value bits << 32 | ~index: larger value, then lower
+// index), NaN skipped, -0 taken as +0 (the reference's `>` treats them as
+// equal). Stage 2: one thread per slot combines its rows' segments and runs
+// the acceptance loop of speculative.h:190-225.
+__global__ void __launch_bounds__(512) qs_argmax_parts_kernel(const void* logits, int dtype, int V, long long row_stride,
+                                                              int segs, int seg_len, unsigned long long* parts) {
+    const int row = blockIdx.x / segs, sg = blockIdx.x % segs;
+    const int lo = sg * seg_len, hi = min(V, lo + seg_len);
+    unsigned long long best = 0ull;
+    auto take = [&](float v, int i) {
+        if (v == v) {
+            const float c = v == 0.0f ? 0.0f : v;
+            const unsigned long long k = ((unsigned long long)qs_key(c) << 32) | (uint32_t)(~(uint32_t)i);
+            best = k > best ? k : best;
+        }
+    };
+    if (dtype == QSAMP_BF16) {
+        const uint16_t* p = (const uint16_t*)logits + (size_t)row * (size_t)row_stride;
+        const bool vec = (((uintptr_t)(p + lo)) % 16) == 0;
+        int i = lo + 8 * threadIdx.x;
+        if (vec)
+            for (; i + 8 <= hi; i += 8 * blockDim.x) {
+                const uint4 q = __ldg((const uint4*)(p + i));
+                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    take(__uint_as_float(w[e] << 16), i + 2 * e);
+                    take(__uint_as_float(w[e] & 0xffff0000u), i + 2 * e + 1);
+                }
+            }
+        for (int j = (vec ? i : lo + threadIdx.x); j < hi; j += (vec ? 1 : blockDim.x)) {
+            if (vec && j >= i + 8) break;
+            take(__uint_as_float((uint32_t)p[j] << 16), j);
+        }
+    } else {
+        const float* p = (const float*)logits + (size_t)row * (size_t)row_stride;
+        const bool vec = (((uintptr_t)(p + lo)) % 16) == 0;
+        int i = lo + 4 * threadIdx.x;
+        if (vec)
+            for (; i + 4 <= hi; i += 4 * blockDim.x) {
+                const float4 q = __ldg((const float4*)(p + i));
+                take(q.x, i); take(q.y, i + 1); take(q.z, i + 2); take(q.w, i + 3);
+            }
+        for (int j = (vec ? i : lo + threadIdx.x); j < hi; j += (vec ? 1 : blockDim.x)) {
+            if (vec && j >= i + 4) break;
+            take(p[j], j);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long y = __shfl_xor_sync(FULLMASK, best, o);
+        best = y > best ? y : best;
+    }
+    __shared__ unsigned long long wb[16];
+    if ((threadIdx.x & 31) == 0) wb[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int q = 1; q < (int)(blockDim.x >> 5); ++q) best = wb[q] > best ? wb[q] : best;
+        parts[blockIdx.x] = best;
+    }
+}
+
+__device__ int verify_argmax(const void* logits, int dtype, long long row_stride, const unsigned long long* parts,
+                             int segs, int row) {
+    float x0;
+    if (dtype == QSAMP_BF16) x0 = __uint_as_float((uint32_t)((const uint16_t*)logits)[(size_t)row * row_stride] << 16);
+    else x0 = ((const float*)logits)[(size_t)row * row_stride];
+    if (x0 != x0) return 0;  // data[0] is NaN: nothing compares larger
+    unsigned long long best = 0ull;
+    for (int q = 0; q < segs; ++q) best = parts[(size_t)row * segs + q] > best ? parts[(size_t)row * segs + q] : best;
+    return (int)(~(uint32_t)best);
+}
+
+__global__ void qs_verify_kernel(const void* logits, int dtype, long long row_stride, const unsigned long long* parts,
+                                 int segs, int B, const int32_t* row_off, const int32_t* drafts, int eos,
+                                 int32_t* out_acc, int32_t* out_bonus, int32_t* out_has) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int r0 = row_off[b], K = row_off[b + 1] - r0;
+    int accepted = 0, bonus = -1, has = 0;
+    if (K == 1) {
+        accepted = 1;
+        bonus = verify_argmax(logits, dtype, row_stride, parts, segs, r0);
+        has = bonus != eos;
+    }
+    for (int i = 0; i < K - 1; ++i) {
+        const int predicted = verify_argmax(logits, dtype, row_stride, parts, segs, r0 + i);
+        if (predicted != drafts[r0 + i + 1]) {
+            accepted = i + 1;
+            bonus = predicted;
+            has = predicted != eos;
+            break;
+        }
+        if (drafts[r0 + i + 1] == eos) {
+            accepted = i + 1;
+            bonus = eos;
+            has = 0;
+            break;
+        }
+        if (i == K - 2) {
+            accepted = K;
+            bonus = verify_argmax(logits, dtype, row_stride, parts, segs, r0 + K - 1);
+            has = bonus != eos;
+        }
+    }
+    out_acc[b] = accepted;
+    out_bonus[b] = bonus;
+    out_has[b] = has;
+}
+
 }  // namespace qs
 
 // launch helpers used by qsamp_api.cu
@@ -2817,6 +2929,21 @@ extern "C" cudaError_t qs_launch_lut(float* lut, float cap, cudaStream_t st) {
 extern "C" size_t qs_stream_smem(int V) { return (size_t)qs::sn_layout(V).total; }
 
 extern "C" size_t qs_merge_smem() { return (size_t)qs::mg_layout().total; }
+extern "C" cudaError_t qs_launch_verify(const void* logits, int dtype, int V, long long row_stride, int n_rows, int B,
+                                        const int32_t* row_off, const int32_t* drafts, int eos, int32_t* out_acc,
+                                        int32_t* out_bonus, int32_t* out_has, unsigned long long* parts, int segs,
+                                        cudaStream_t st) {
+    int seg_len = (V + segs - 1) / segs;
+    seg_len = (seg_len + 7) / 8 * 8;  // segment starts stay 16-byte aligned with the row
+    if (n_rows > 0) {
+        qs::qs_argmax_parts_kernel<<<n_rows * segs, 512, 0, st>>>(logits, dtype, V, row_stride, segs, seg_len, parts);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    qs::qs_verify_kernel<<<(B + 127) / 128, 128, 0, st>>>(logits, dtype, row_stride, parts, segs, B, row_off, drafts,
+                                                          eos, out_acc, out_bonus, out_has);
+    return cudaGetLastError();
+}
 extern "C" cudaError_t qs_launch_char_class(const uint16_t* table, int V, int B, const uint32_t* classes,
                                             uint32_t* masks, long long mask_stride, int or_into, int num_sms,
                                             cudaStream_t st) {

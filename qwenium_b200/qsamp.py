@@ -63,7 +63,7 @@ EXPORTS = (
     "qsamp_create", "qsamp_destroy", "qsamp_last_error", "qsamp_sample", "qsamp_sample_host",
     "qsamp_pack_ids", "qsamp_grammar_mask", "qsamp_find_eos_string", "qsamp_keep_list_mask",
     "qsamp_mask_and", "qsamp_shard_topk", "qsamp_merge_topk", "qsamp_get_counters", "qsamp_set_kernel_timing",
-    "qsamp_sample_static", "qsamp_first_byte_table", "qsamp_char_class_masks",
+    "qsamp_sample_static", "qsamp_first_byte_table", "qsamp_char_class_masks", "qsamp_verify_greedy",
 )
 
 _P = ctypes.c_void_p
@@ -152,6 +152,9 @@ def load(path: str = LIB_PATH):
                                      ctypes.c_uint64, _P, _P, _P]
     lib.qsamp_get_counters.restype = ctypes.c_int
     lib.qsamp_get_counters.argtypes = [_P, ctypes.POINTER(_Counters)]
+    lib.qsamp_verify_greedy.restype = ctypes.c_int
+    lib.qsamp_verify_greedy.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
+                                        ctypes.c_int32, _P, _P, ctypes.c_int32, _P, _P, _P, _P]
     lib.qsamp_first_byte_table.restype = ctypes.c_int
     lib.qsamp_first_byte_table.argtypes = [_P, _P, ctypes.c_int32, _P]
     lib.qsamp_char_class_masks.restype = ctypes.c_int
@@ -292,6 +295,26 @@ class Context:
     def set_kernel_timing(self, on: bool):
         """Bracket each selection kernel with CUDA events (see counters())."""
         self._check(self.lib.qsamp_set_kernel_timing(self.h, 1 if on else 0), "qsamp_set_kernel_timing")
+
+    def verify_greedy(self, logits, row_off, drafts, eos_token: int = -1, stream=None):
+        """qsamp_verify_greedy on CUDA tensors: logits [n_rows][V] (fp32, or
+        bf16 bits as int16/bfloat16), row_off int32 [B+1], drafts int32
+        [n_rows]. Returns (accepted, bonus, has_bonus) int32 [B] tensors."""
+        import torch
+
+        n_rows, V = int(logits.shape[0]), int(logits.shape[1])
+        B = int(row_off.shape[0]) - 1
+        dtype = QSAMP_BF16 if logits.dtype in (torch.bfloat16, torch.int16, torch.uint16) else QSAMP_F32
+        acc = torch.empty(B, dtype=torch.int32, device=row_off.device)
+        bonus = torch.empty_like(acc)
+        has = torch.empty_like(acc)
+        if stream is None:
+            stream = torch.cuda.current_stream(row_off.device).cuda_stream
+        self._check(self.lib.qsamp_verify_greedy(self.h, _dev_ptr(logits), dtype, V, int(logits.stride(0)), n_rows, B,
+                                                 _dev_ptr(row_off), _dev_ptr(drafts), int(eos_token), _dev_ptr(acc),
+                                                 _dev_ptr(bonus), _dev_ptr(has), ctypes.c_void_p(stream)),
+                    "qsamp_verify_greedy")
+        return acc, bonus, has
 
     def char_class_masks(self, table, classes, masks, or_into: bool = False, stream=None):
         """qsamp_char_class_masks on CUDA tensors: table uint16 [V] (as int16),
