@@ -2773,20 +2773,34 @@ __global__ void __launch_bounds__(512) qs_argmax_parts_kernel(const void* logits
                                                               int segs, int seg_len, unsigned long long* parts) {
     const int row = blockIdx.x / segs, sg = blockIdx.x % segs;
     const int lo = sg * seg_len, hi = min(V, lo + seg_len);
-    unsigned long long best = 0ull;
+    // Each thread meets its elements in increasing index order, so `v > bv`
+    // keeps the first maximum (NaN never compares larger; -0 == +0).
+    float bv = -__int_as_float(0x7f800000);
+    int bi = 0x7fffffff;
     auto take = [&](float v, int i) {
-        if (v == v) {
-            const float c = v == 0.0f ? 0.0f : v;
-            const unsigned long long k = ((unsigned long long)qs_key(c) << 32) | (uint32_t)(~(uint32_t)i);
-            best = k > best ? k : best;
-        }
+        if (v > bv || (bi == 0x7fffffff && v == bv)) { bv = v; bi = i; }
     };
     if (dtype == QSAMP_BF16) {
         const uint16_t* p = (const uint16_t*)logits + (size_t)row * (size_t)row_stride;
         const bool vec = (((uintptr_t)(p + lo)) % 16) == 0;
         int i = lo + 8 * threadIdx.x;
-        if (vec)
-            for (; i + 8 <= hi; i += 8 * blockDim.x) {
+        if (vec) {
+            const int step = 8 * blockDim.x;
+            for (; i + step + 8 <= hi; i += 2 * step) {  // two 16-byte loads in flight
+                const uint4 q0 = __ldg((const uint4*)(p + i)), q1 = __ldg((const uint4*)(p + i + step));
+                const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w}, w1[4] = {q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    take(__uint_as_float(w0[e] << 16), i + 2 * e);
+                    take(__uint_as_float(w0[e] & 0xffff0000u), i + 2 * e + 1);
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    take(__uint_as_float(w1[e] << 16), i + step + 2 * e);
+                    take(__uint_as_float(w1[e] & 0xffff0000u), i + step + 2 * e + 1);
+                }
+            }
+            for (; i + 8 <= hi; i += step) {
                 const uint4 q = __ldg((const uint4*)(p + i));
                 const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -2795,24 +2809,35 @@ __global__ void __launch_bounds__(512) qs_argmax_parts_kernel(const void* logits
                     take(__uint_as_float(w[e] & 0xffff0000u), i + 2 * e + 1);
                 }
             }
-        for (int j = (vec ? i : lo + threadIdx.x); j < hi; j += (vec ? 1 : blockDim.x)) {
-            if (vec && j >= i + 8) break;
-            take(__uint_as_float((uint32_t)p[j] << 16), j);
+            for (int j = i; j < hi && j < i + 8; ++j) take(__uint_as_float((uint32_t)p[j] << 16), j);
+        } else {
+            for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) take(__uint_as_float((uint32_t)p[j] << 16), j);
         }
     } else {
         const float* p = (const float*)logits + (size_t)row * (size_t)row_stride;
         const bool vec = (((uintptr_t)(p + lo)) % 16) == 0;
         int i = lo + 4 * threadIdx.x;
-        if (vec)
-            for (; i + 4 <= hi; i += 4 * blockDim.x) {
+        if (vec) {
+            const int step = 4 * blockDim.x;
+            for (; i + step + 4 <= hi; i += 2 * step) {  // two 16-byte loads in flight
+                const float4 q0 = __ldg((const float4*)(p + i)), q1 = __ldg((const float4*)(p + i + step));
+                take(q0.x, i); take(q0.y, i + 1); take(q0.z, i + 2); take(q0.w, i + 3);
+                take(q1.x, i + step); take(q1.y, i + step + 1); take(q1.z, i + step + 2); take(q1.w, i + step + 3);
+            }
+            for (; i + 4 <= hi; i += step) {
                 const float4 q = __ldg((const float4*)(p + i));
                 take(q.x, i); take(q.y, i + 1); take(q.z, i + 2); take(q.w, i + 3);
             }
-        for (int j = (vec ? i : lo + threadIdx.x); j < hi; j += (vec ? 1 : blockDim.x)) {
-            if (vec && j >= i + 4) break;
-            take(p[j], j);
+            for (int j = i; j < hi && j < i + 4; ++j) take(p[j], j);
+        } else {
+            for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) take(p[j], j);
         }
     }
+    // across threads: the larger value, then the lower index (keys as below)
+    unsigned long long best = bi == 0x7fffffff
+                                  ? 0ull
+                                  : (((unsigned long long)qs_key(bv == 0.0f ? 0.0f : bv) << 32) |
+                                     (uint32_t)(~(uint32_t)bi));
     for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long y = __shfl_xor_sync(FULLMASK, best, o);
         best = y > best ? y : best;
