@@ -1391,12 +1391,19 @@ __device__ void predict_s(const Sm& s, int from, double ratio) {
 
 // CTA 0: top-p walk predictions for bins >= from (cum ~ prefix(t) / S_n,
 // scaled by `ratio`); bins at a binade change or near top_p are gathered.
-__device__ void predict_c(const Sm& s, int from, double ratio, float top_p) {
+// u: the row's uniform. Besides the cumulative walk's own needs, the bins
+// around the predicted draw position (cum ~ u * top_p of the survivors'
+// mass) are gathered in the same pass, so that the draw rarely needs one.
+__device__ void predict_c(const Sm& s, int from, double ratio, float top_p, double u) {
     Misc* m = s.misc;
     const double Sn = m->S_n;
     block_bin_prefix<double>([&](int b) { return b < NB - 1 ? (double)TX(b) * 0x1p-40 : 0.0; }, s.pref, m,
                              (double*)nullptr);
-    const double D = 2e-3, pp = top_p;
+    // D: margin of the binade predictions; Dc, Dd: windows around the
+    // predicted cut and draw. A miss costs one more pass, never a wrong
+    // result (the walk verifies every bin); a wide window in a sparse tail
+    // would gather thousands of elements.
+    const double D = 2e-3, Dc = 2e-4, Dd = 5e-4, pp = top_p;
     int bmax = -1;
     for (int b = threadIdx.x; b < NB; b += NT) {
         uint8_t f = (uint8_t)(s.flag[b] & ~(F_PLAINC | F_WANT));
@@ -1405,9 +1412,11 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p) {
             if (ca <= pp + 1e-2) {
                 bmax = b > bmax ? b : bmax;
                 const bool crossing = !(ca > 0) || binade_d(ca * (1 - D)) != binade_d(cb * (1 + D));
-                const bool cut = cb >= pp - D && ca <= pp + D;
-                if ((crossing || cut || b == from) && !RUNBIN(b)) f |= F_WANT;
-                else { f |= F_PLAINC; s.gc[b] = (int8_t)binade_d(ca > 0 ? ca : 1.0); }
+                const bool cut = cb >= pp - Dc && ca <= pp + Dc;
+                const double dt = u * pp;
+                const bool draw = cb >= dt - Dd && ca <= dt + Dd && (int)s.cnt[b] <= SPEC_CAP / 2;
+                if (((crossing || cut || b == from) && !RUNBIN(b)) || draw) f |= F_WANT;
+                if (!(f & F_WANT) || RUNBIN(b)) { f |= F_PLAINC; s.gc[b] = (int8_t)binade_d(ca > 0 ? ca : 1.0); }
             }
         }
         s.flag[b] = f;
@@ -1516,14 +1525,11 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     want = binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
                 }
                 const double ca = Pa / S_est, cb = Pb / S_est;
-                if (pa) {
-                    if (cb >= pp - D && ca <= pp + D) want = true;
-                    if (ca > 0 && ca <= pp + D && binade_d(ca * (1 - D)) != binade_d(cb * (1 + D))) want = true;
-                }
                 if (RUNBIN(b)) want = false;
-                // ... and ids: the predicted draw and the top list
+                // ... and ids: the predicted draw (rows without top-p: the
+                // cumulative pass of a top-p row gathers its own) and the top list
                 const double tgt = u * pp;
-                if (cb >= tgt - D && ca <= tgt + D) want = true;
+                if (!pa && cb >= tgt - D && ca <= tgt + D) want = true;
                 if ((long long)cpre[b] < topn) want = true;
                 f = want ? F_WANT : F_PLAINS;
             }
@@ -1718,7 +1724,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         go = true;
                     }
                 } else if (stage == ST_CUMPREP) {
-                    predict_c(s, 0, 1.0, p.top_p);
+                    predict_c(s, 0, 1.0, p.top_p, row_u(a, r.row, p));
                     if (threadIdx.x == 0) {
                         w.stage = ST_CUMWALK;
                         w.need = 0;  // a pass (bin 0 is gathered again)
@@ -1834,7 +1840,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         const double P = s.pref[fb] / (double)Sn;
                         const double ratio = P > 0.0 ? (double)w.C / P : 1.0;
                         __syncthreads();
-                        predict_c(s, fb, ratio, p.top_p);
+                        predict_c(s, fb, ratio, p.top_p, row_u(a, r.row, p));
                     } else {
                         if (w.stage == ST_DRAW && !w.cut_all) {
                             int part = 0;
