@@ -252,6 +252,8 @@ def run_gpu(args):
         t10 = a.elapsed_time(b) / n10
         b10 = {"ms_per_step": round(t10, 4), "rows_per_s": round(10 / (t10 * 1e-3), 1)}
 
+    extras = run_extras(ctx, dev, stream) if (rank == 0 and args.extras) else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(cfg, seconds=args.cpu_seconds)
@@ -299,9 +301,95 @@ def run_gpu(args):
     }
     if b10:
         out["b10"] = b10
+    if extras:
+        out["extras"] = extras
     if cpu:
         out["cpu_baseline"] = cpu
     print(json.dumps(out))
+
+
+def _events_ms(stream, fn, reps):
+    import torch
+
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(reps):
+        fn(i)
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_extras(ctx, dev, stream):
+    """Secondary measurements (device-timed, inputs resident, rotating buffers):
+    C4 (bf16 V=262144, soft-cap, full-vocabulary top-p), batched greedy draft
+    verification and grammar char-class masks; with the reference's own CPU
+    time per unit where it compiled (oracle/_ref)."""
+    import ctypes
+
+    import torch
+
+    from qwenium_b200 import qsamp
+    from qwenium_b200 import workloads as W
+
+    out = {}
+    peak, _ = measured_peaks()
+    # C4 at B=256: every row takes the cluster kernel
+    c4 = W.config4(4, B=256)
+    xs = [torch.from_numpy(np.ascontiguousarray(c4["logits"]).view(np.int16)).to(dev) for _ in range(2)]
+    h4 = torch.from_numpy(c4["hist"]).to(dev)
+    f4 = lambda i: ctx.sample_batch(xs[i % 2], c4["params"], hist=h4, hist_len=c4["hist_len"], u=c4["u"],
+                                    stream=stream.cuda_stream)
+    for i in range(3):
+        f4(i)
+    ms = _events_ms(stream, f4, 5)
+    out["config4_B256"] = {"ms_per_call": round(ms, 4), "rows_per_s": round(256 / (ms * 1e-3), 1)}
+    # greedy verification: 128 slots x 5 drafts, V=151936 fp32
+    rng = np.random.default_rng(0)
+    n, K = 640, 5
+    vx = [torch.from_numpy((rng.standard_normal((n, V)) * 3).astype(np.float32)).to(dev) for _ in range(3)]
+    off = torch.from_numpy(np.arange(0, n + 1, K, dtype=np.int32)).to(dev)
+    dr = torch.from_numpy(rng.integers(0, V, n).astype(np.int32)).to(dev)
+    fv = lambda i: ctx.verify_greedy(vx[i % 3], off, dr, -1, stream=stream.cuda_stream)
+    for i in range(3):
+        fv(i)
+    ms = _events_ms(stream, fv, 20)
+    gbs = n * V * 4 / (ms * 1e-3) / 1e9
+    out["verify_greedy"] = {"rows": n, "V": V, "us_per_call": round(ms * 1e3, 1), "gbs": round(gbs, 1),
+                            "frac_of_measured_hbm": round(gbs / peak, 3)}
+    # char-class masks: 256 states, negated class [^"\\] over the C3 vocabulary
+    vocab = W.config3_vocab()
+    table = qsamp.first_byte_table(vocab)
+    cls = np.stack([qsamp.char_class_bits(['"', "\\"], True) for _ in range(256)])
+    dt = torch.from_numpy(table.view(np.int16)).to(dev)
+    dc = torch.from_numpy(cls.view(np.int32)).to(dev)
+    dm = torch.zeros((256, (len(vocab) + 31) // 32), dtype=torch.int32, device=dev)
+    fc = lambda i: ctx.char_class_masks(dt, dc, dm, stream=stream.cuda_stream)
+    for i in range(3):
+        fc(i)
+    ms = _events_ms(stream, fc, 50)
+    out["char_class_masks"] = {"states": 256, "V": len(vocab), "us_per_call": round(ms * 1e3, 2)}
+    # the reference's per-unit CPU times (one host thread), where it compiled
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    if O.ref_available("strict"):
+        lib = O.ref_lib("strict")
+        x5 = (rng.standard_normal((K, V)) * 3).astype(np.float32)
+        d5 = np.arange(K, dtype=np.int32)
+        a_, b_, h_ = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        t0 = time.perf_counter()
+        for _ in range(20):
+            lib.qwref_spec_verify(O._ptr(x5), K, V, O._ptr(d5), -1, ctypes.byref(a_), ctypes.byref(b_), ctypes.byref(h_))
+        out["verify_greedy"]["reference_us_per_slot"] = round((time.perf_counter() - t0) / 20 * 1e6, 1)
+        rv = O.RefVocab(vocab)
+        arr = np.frombuffer(b'"\\', np.uint8).copy()
+        mk = np.zeros(len(vocab), np.uint8)
+        t0 = time.perf_counter()
+        for _ in range(20):
+            lib.qwref_trie_mark_char_class(rv.trie, O._ptr(arr), 2, 1, len(vocab), O._ptr(mk))
+        out["char_class_masks"]["reference_us_per_state"] = round((time.perf_counter() - t0) / 20 * 1e6, 1)
+    return out
 
 
 # ------------------------------------------------------------------ CPU legs
@@ -418,6 +506,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-b10", action="store_true")
+    ap.add_argument("--extras", action="store_true",
+                    help="also time C4 (bf16, V=262144), draft verification and char-class masks (rank 0)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
