@@ -460,6 +460,18 @@ __device__ int warp_walk_terms(float& S, int n, float stop, TermF term) {
     return n;
 }
 
+// The first bin from which no element can change a running sum S > 0: every
+// element of bin b has t <= e^{-(b-1)/R} (b = floor(-x R) up to the rounding
+// of that product, and expf within an ulp), so bins with e^{-(b-1)/R} below
+// half an ulp of S add exactly nothing. Two bins of margin on top.
+__device__ __forceinline__ int s_dead_bin(float S) {
+    const int e = binade(S);                                   // S in [2^e, 2^(e+1))
+    const double lnh = (double)(e - 24) * 0.69314718055994531;  // ln(ulp(S) / 2)
+    const double bb = 1.0 - (double)BIN_R * lnh;               // e^{-(b-1)/R} < h  <=>  b > bb
+    const long long d = (long long)bb + 3;
+    return d > NB - 1 ? NB - 1 : (int)d;
+}
+
 // One full warp advances S over bins [b, bend) whose k-sums (at binade g[b])
 // are valid for the current S; stops at the first bin that needs its
 // elements (returned), or at bend. Optionally records S at each bin start.
@@ -1668,8 +1680,15 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         float S = w.S;
                         int b = w.swb;
                         while (true) {
-                            b = warp_walk_bins(S, b, NB - 1, s, s.gs, F_PLAINS, POS_INF, true);
-                            if (b >= NB - 1) break;
+                            // bins from `dead` on cannot change S (their largest term is
+                            // below half an ulp of S): the walk ends there
+                            const int dead = S > 0.0f ? s_dead_bin(S) : NB - 1;
+                            b = warp_walk_bins(S, b, dead, s, s.gs, F_PLAINS, POS_INF, true);
+                            if (b >= dead) {
+                                for (int q = b + lane; q < NB - 1; q += 32) s.sstart[q] = S;
+                                b = NB - 1;
+                                break;
+                            }
                             if (RUNBIN(b)) {
                                 // one or two runs of equal terms: closed form
                                 if (threadIdx.x == 0) {
