@@ -475,9 +475,14 @@ __device__ __forceinline__ int s_dead_bin(float S) {
 // One full warp advances S over bins [b, bend) whose k-sums (at binade g[b])
 // are valid for the current S; stops at the first bin that needs its
 // elements (returned), or at bend. Optionally records S at each bin start.
+// The k-sums are read as the exclusive prefix E = s.ksum over the last pass's
+// bin range (prefix_ksums), so within one binade of S the sum after bin b is
+// m + E[b+1] - E[b0] ulps with no dependence between 32-bin chunks.
 __device__ int warp_walk_bins(float& S, int b, int bend, const Sm& s, const int8_t* g, uint8_t plain_bit,
                               float stop, bool record) {
     const int lane = threadIdx.x & 31;
+    const unsigned long long* E = s.ksum;
+    const unsigned long long lim = 1ull << 24;
     while (b < bend) {
         if (!(S > 0.0f)) {
             // an empty bin before the first element leaves S at 0
@@ -492,36 +497,29 @@ __device__ int warp_walk_bins(float& S, int b, int bend, const Sm& s, const int8
         }
         const int e = binade(S);
         const float down = pow2f(e - 23);
-        const uint32_t m = (uint32_t)__fmul_rn(S, pow2f(23 - e));
-        const int bb = b + lane;
-        bool plain = false;
-        unsigned long long k = 0;
-        if (bb < bend) {
-            const uint32_t c = s.cnt[bb];
-            if (c == 0) {
-                plain = true;
-            } else {
+        const unsigned long long m = (uint32_t)__fmul_rn(S, pow2f(23 - e));
+        const unsigned long long e0 = E[b];
+        while (b < bend) {
+            const int bb = b + lane;
+            bool ok = false;
+            float before = 0.0f, after = 0.0f;
+            if (bb < bend) {
+                const uint32_t c = s.cnt[bb];
+                const uint8_t f = s.flag[bb];
                 const bool tied = (s.tie[bb >> 5] >> (bb & 31)) & 1u;
-                plain = (s.flag[bb] & plain_bit) && !(s.flag[bb] & F_GATH) && g[bb] == e && !tied;
-                if (plain) k = KSUM(bb);
+                const bool plain = c == 0 || ((f & plain_bit) && !(f & F_GATH) && g[bb] == e && !tied);
+                const unsigned long long pa = m + (E[bb] - e0), pb = m + (E[bb + 1] - e0);
+                if (pa <= lim) before = __fmul_rn((float)pa, down);
+                if (pb <= lim) after = __fmul_rn((float)pb, down);
+                ok = plain && pa < lim && pb <= lim && !(after >= stop);
             }
+            const uint32_t okm = __ballot_sync(FULLMASK, ok);
+            const int L = (okm == FULLMASK) ? 32 : (__ffs(~okm) - 1);
+            if (record && lane <= L && bb < bend) s.sstart[bb] = before;
+            if (L > 0) S = __shfl_sync(FULLMASK, after, L - 1);
+            b += L;
+            if (L < 32) return b < bend ? b : bend;
         }
-        unsigned long long pre = k;
-        for (int o = 1; o < 32; o <<= 1) {
-            const unsigned long long v = __shfl_up_sync(FULLMASK, pre, o);
-            if (lane >= o) pre += v;
-        }
-        const unsigned long long prev = pre - k;
-        const unsigned long long lim = 1ull << 24;
-        const float before = (m + prev <= lim) ? __fmul_rn((float)(m + prev), down) : 0.0f;
-        const float after = (m + pre <= lim) ? __fmul_rn((float)(m + pre), down) : 0.0f;
-        const bool ok = bb < bend && plain && (m + prev < lim) && (m + pre <= lim) && !(after >= stop);
-        const uint32_t okm = __ballot_sync(FULLMASK, ok);
-        const int L = (okm == FULLMASK) ? 32 : (__ffs(~okm) - 1);
-        if (record && lane <= L && bb < bend) s.sstart[bb] = before;
-        if (L > 0) S = __shfl_sync(FULLMASK, after, L - 1);
-        b += L;
-        if (L < 32) return b < bend ? b : bend;
     }
     return bend;
 }
@@ -1653,6 +1651,13 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
         }
         if (it_no < 5) QS_TMARK(r.row, 9 + 3 * it_no, rank == 0);
         if (rank == 0) {
+            if (m->kmode) {
+                // the walks read the pass's k-sums as an exclusive prefix over its range
+                const int kf = m->kfrom, kt = m->kto;
+                block_bin_prefix<unsigned long long>(
+                    [&](int b) { return (b >= kf && b <= kt) ? KSUM(b) : 0ull; }, s.ksum, m,
+                    (unsigned long long*)nullptr);
+            }
             {
                 const int n = m->spec_n < SPEC_CAP ? m->spec_n : SPEC_CAP;
                 const int P2 = next_pow2(n > 1 ? n : 1);
