@@ -472,14 +472,17 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         if (!st_ok) c->h_rows[(size_t)j++] = r, ++n_cluster;
     }
     // Cluster rows are served from a queue in list order: the ones likely to
-    // need the most gather rounds go first (a top-p cutoff, deeper p first),
-    // so that they do not start last and set the kernel's length.
-    // When rows arrive in chunks, rows of earlier chunks go first.
+    // take longest go first, so that they do not start last and set the
+    // kernel's length. A higher temperature flattens the row (more logits
+    // within reach of the maximum: heavier passes and walks), a top-p cutoff
+    // adds the cumulative walk; the key is the temperature, plus one for a
+    // cutoff. When rows arrive in chunks, rows of earlier chunks go first.
     std::stable_sort(c->h_rows.begin() + n_stream, c->h_rows.begin() + n_stream + n_cluster, [&](int x, int y) {
         if (ready_rows > 0 && x / ready_rows != y / ready_rows) return x / ready_rows < y / ready_rows;
         auto key = [&](int r) {
-            const float tp = b->params[r].top_p;
-            return (tp > 0.0f && tp < 1.0f) ? tp : 0.0f;
+            const qsamp_row_params& p = b->params[r];
+            const float T = p.temperature > 0.0f ? p.temperature : 0.0f;
+            return T + ((p.top_p > 0.0f && p.top_p < 1.0f) ? 1.0f : 0.0f);
         };
         return key(x) > key(y);
     });

@@ -1402,8 +1402,12 @@ __device__ void predict_s(const Sm& s, int from, double ratio) {
 // CTA 0: top-p walk predictions for bins >= from (cum ~ prefix(t) / S_n,
 // scaled by `ratio`); bins at a binade change or near top_p are gathered.
 // u: the row's uniform. Besides the cumulative walk's own needs, the bins
-// around the predicted draw position (cum ~ u * top_p of the survivors'
-// mass) are gathered in the same pass, so that the draw rarely needs one.
+// around the predicted draw position are gathered in the same pass, so that
+// the draw rarely needs one: the draw's target is u times the kept mass,
+// which lies between top_p and top_p plus the largest probability of an
+// element of the first bin that may hold the cut. On a re-prediction
+// (from > 0) the draw bins before `from` are wanted again (every pass
+// rebuilds the gathered list).
 __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, double u) {
     Misc* m = s.misc;
     const double Sn = m->S_n;
@@ -1414,19 +1418,35 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, doub
     // result (the walk verifies every bin); a wide window in a sparse tail
     // would gather thousands of elements.
     const double D = 2e-3, Dc = 2e-4, Dd = 5e-4, pp = top_p;
+    __shared__ int pc_bcut;
+    if (threadIdx.x == 0) pc_bcut = NB - 1;
+    __syncthreads();
+    for (int b = threadIdx.x; b < NB - 1; b += NT) {
+        if (s.cnt[b] == 0) continue;
+        const double ca = s.pref[b] / Sn * ratio, cb = (s.pref[b] + (double)TX(b) * 0x1p-40) / Sn * ratio;
+        if (cb >= pp - Dc && ca <= pp + Dc) atomicMin(&pc_bcut, b);
+    }
+    __syncthreads();
+    const int bcut = pc_bcut;
+    // every element of bin b has t <= e^{-(b-1)/R} (the bound s_dead_bin uses)
+    const double pmax = bcut < NB - 1 ? exp(-(double)(bcut - 1) / (double)BIN_R) / Sn : 1.0;
+    const double dlo = u * pp - Dd, dhi = u * (pp + pmax) + Dd;
     int bmax = -1;
     for (int b = threadIdx.x; b < NB; b += NT) {
         uint8_t f = (uint8_t)(s.flag[b] & ~(F_PLAINC | F_WANT));
-        if (b >= from && b < NB - 1 && s.cnt[b] > 0) {
+        if (b < NB - 1 && s.cnt[b] > 0) {
             const double ca = s.pref[b] / Sn * ratio, cb = (s.pref[b] + (double)TX(b) * 0x1p-40) / Sn * ratio;
-            if (ca <= pp + 1e-2) {
-                bmax = b > bmax ? b : bmax;
-                const bool crossing = !(ca > 0) || binade_d(ca * (1 - D)) != binade_d(cb * (1 + D));
-                const bool cut = cb >= pp - Dc && ca <= pp + Dc;
-                const double dt = u * pp;
-                const bool draw = cb >= dt - Dd && ca <= dt + Dd && (int)s.cnt[b] <= SPEC_CAP / 2;
-                if (((crossing || cut || b == from) && !RUNBIN(b)) || draw) f |= F_WANT;
-                if (!(f & F_WANT) || RUNBIN(b)) { f |= F_PLAINC; s.gc[b] = (int8_t)binade_d(ca > 0 ? ca : 1.0); }
+            const bool draw = cb >= dlo && ca <= dhi && (int)s.cnt[b] <= SPEC_CAP / 2;
+            if (b >= from) {
+                if (ca <= pp + 1e-2) {
+                    bmax = b > bmax ? b : bmax;
+                    const bool crossing = !(ca > 0) || binade_d(ca * (1 - D)) != binade_d(cb * (1 + D));
+                    const bool cut = cb >= pp - Dc && ca <= pp + Dc;
+                    if (((crossing || cut || b == from) && !RUNBIN(b)) || draw) f |= F_WANT;
+                    if (!(f & F_WANT) || RUNBIN(b)) { f |= F_PLAINC; s.gc[b] = (int8_t)binade_d(ca > 0 ? ca : 1.0); }
+                }
+            } else if (draw) {
+                f |= F_WANT;
             }
         }
         s.flag[b] = f;
