@@ -2263,7 +2263,8 @@ constexpr int SN_CAP = KMAX + 2 * SN_CH;   // candidate buffer entries
 constexpr int SN_SLACK = 256;              // compaction once k + SN_SLACK are held
 constexpr int SN_HMAX = 1024;              // penalty window this kernel takes
 constexpr int SN_HT = 2 * SN_HMAX;         // window hash table slots (power of two)
-static_assert(SN_PER == 4 && SN_CAP % SN_NT == 0, "stream kernel shape");
+constexpr int SN_G = 4;                    // chunks per super-chunk (one barrier each)
+static_assert(SN_PER == 4 && SN_G * SN_PER <= 32 && SN_CAP % SN_NT == 0, "stream kernel shape");
 static_assert(KMAX + SN_SLACK + SN_CH + SN_HMAX <= SN_CAP, "candidate buffer bound");
 
 struct SnLayout {
@@ -2415,6 +2416,27 @@ __device__ unsigned long long sn_compact(unsigned long long* cand, int& n, int k
     return ck;
 }
 
+// One warp step of candidate appends: lanes with ok reserve slots together;
+// a slot at or past cap is not written and the lane is told so (its element
+// waits for the next compaction). over: the list passed trig.
+__device__ __forceinline__ bool sn_append(unsigned long long* cand, int* n, int cap, int trig, bool ok,
+                                          unsigned long long cc, bool& over) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t bal = __ballot_sync(FULLMASK, ok);
+    if (!bal) return false;
+    int base = 0;
+    if (lane == 0) base = atomicAdd(n, __popc(bal));
+    base = __shfl_sync(FULLMASK, base, 0);
+    over |= base + __popc(bal) > trig;
+    if (!ok) return false;
+    const int slot = base + __popc(bal & ((1u << lane) - 1u));
+    if (slot < cap) {
+        cand[slot] = cc;
+        return false;
+    }
+    return true;
+}
+
 // The SN_PER consecutive elements from i0 (raw logits and bf16 bits).
 __device__ __forceinline__ void sn_load(const RowCtx& r, bool vec, int i0, int V, float (&x)[SN_PER],
                                         uint32_t (&b)[SN_PER]) {
@@ -2481,7 +2503,6 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
     const int V = a.V;
     const int words = (V + 31) / 32;
     const float NEG_INF = -__int_as_float(0x7f800000);
-    const int lane = threadIdx.x & 31;
     for (int w = threadIdx.x; w < words; w += SN_NT) bitmap[w] = 0u;
     __shared__ int sh_nuniq, sh_n;
     __shared__ unsigned long long sh_tau;
@@ -2563,6 +2584,10 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
         const bool vec = a.vec_ok != 0;  // 16-byte aligned rows
         const int nchunks = (V + SN_CH - 1) / SN_CH;
         const int trig = min(k + SN_SLACK, SN_CAP - SN_CH);
+        const int cap = SN_CAP - SN_HMAX;  // streamed candidates (the window's ids follow)
+        bool over = false;                 // since the last barrier the list passed trig
+        uint32_t pend = 0u;                // passing elements of this super-chunk that found the list full
+        int sc_first = 0;                  // the super-chunk's first chunk
         const int j0 = SN_PER * threadIdx.x;
         float xn[SN_PER];
         uint32_t bn[SN_PER];
@@ -2594,15 +2619,16 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
 #pragma unroll
                 for (int e = 0; e < SN_PER; ++e)
                     if (i0 + e < V && !(x[e] < xt)) lm |= 1u << e;
-                bool over = false;
+                const int g = c - sc_first;  // sub-chunk of the current super-chunk
                 if (__any_sync(FULLMASK, lm != 0u)) {
                     if (nuniq && lm) lm &= ~(bitmap[i0 >> 5] >> (i0 & 31));  // window ids: folded in later
                     const unsigned long long tau = sh_tau;
                     while (__any_sync(FULLMASK, lm != 0u)) {
                         bool ok = false;
                         unsigned long long cc = 0ull;
+                        int e = 0;
                         if (lm) {
-                            const int e = __ffs((int)lm) - 1;
+                            e = __ffs((int)lm) - 1;
                             lm &= lm - 1u;
                             const float xv = e == 0 ? x[0] : (e == 1 ? x[1] : (e == 2 ? x[2] : x[3]));
                             const uint32_t hv = e == 0 ? b16[0] : (e == 1 ? b16[1] : (e == 2 ? b16[2] : b16[3]));
@@ -2610,23 +2636,40 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
                             cc = composite(v, i0 + e);
                             ok = cc > tau;
                         }
-                        const uint32_t bal = __ballot_sync(FULLMASK, ok);
-                        if (bal) {
-                            int base = 0;
-                            if (lane == 0) base = atomicAdd(&sh_n, __popc(bal));
-                            base = __shfl_sync(FULLMASK, base, 0);
-                            if (ok) cand[base + __popc(bal & ((1u << lane) - 1u))] = cc;
-                            over |= base + __popc(bal) > trig;
-                        }
+                        if (sn_append(cand, &sh_n, cap, trig, ok, cc, over)) pend |= 1u << (g * SN_PER + e);
                     }
                 }
-                // the appender that crossed the trigger knows it: the decision
-                // is the barrier's own OR, identical in every thread
-                if (__syncthreads_or(over)) {
-                    int n = sh_n;
-                    const unsigned long long ck = sn_compact(cand, n, k, hist, m);
-                    if (threadIdx.x == 0) { sh_tau = ck; sh_n = n; sh_xthr = raw_lower_bound(r, comp_val(ck)); }
-                    __syncthreads();
+                // a super-chunk ends with the row's first chunk, every SN_G
+                // chunks and with the row: the list is compacted there when
+                // an appender crossed the trigger (the barrier's own OR, the
+                // same in every thread), and elements that found it full are
+                // filtered again against the new threshold
+                if (c == 0 || g == SN_G - 1 || c == nchunks - 1) {
+                    while (__syncthreads_or(over)) {
+                        int n = sh_n < cap ? sh_n : cap;
+                        const unsigned long long ck = sn_compact(cand, n, k, hist, m);
+                        if (threadIdx.x == 0) { sh_tau = ck; sh_n = n; sh_xthr = raw_lower_bound(r, comp_val(ck)); }
+                        __syncthreads();
+                        over = false;
+                        uint32_t pm = pend;
+                        pend = 0u;
+                        while (__any_sync(FULLMASK, pm != 0u)) {
+                            bool ok = false;
+                            unsigned long long cc = 0ull;
+                            int q = 0;
+                            if (pm) {
+                                q = __ffs((int)pm) - 1;
+                                pm &= pm - 1u;
+                                const int i = (sc_first + q / SN_PER) * SN_CH + j0 + (q % SN_PER);
+                                const uint32_t hv = r.dtype == QSAMP_BF16 ? ((const uint16_t*)r.rowp)[i] : 0u;
+                                const float v = post_value(r, pre_value(r, i, raw_at(r, i), hv));
+                                cc = composite(v, i);
+                                ok = cc > ck;
+                            }
+                            if (sn_append(cand, &sh_n, cap, trig, ok, cc, over)) pend |= 1u << q;
+                        }
+                    }
+                    sc_first = c + 1;
                 }
             }
         }

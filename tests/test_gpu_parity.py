@@ -166,3 +166,43 @@ def test_all_masked_and_forced(ctx, oracle_mod):
     cfg["params"]["force_token"] = [-1, 7, -1, 999]
     cfg["params"]["temperature"] = [0.0, 0.8, 1.0, 0.0]
     check(ctx, oracle_mod, cfg)
+
+
+def _order_cfg(kind, V, ks, bf16=False, seed=11):
+    """Rows whose order defeats a running top-k threshold: ascending values
+    (every element beats the list so far), descending, all equal (ties by id),
+    and ascending runs; the stream's candidate list overflows and is compacted
+    many times per row."""
+    rng = np.random.default_rng(seed)
+    B = len(ks)
+    x = np.empty((B, V), np.float32)
+    for b in range(B):
+        if kind == "ascending":
+            x[b] = np.linspace(-20.0, 20.0, V, dtype=np.float32)
+        elif kind == "descending":
+            x[b] = np.linspace(20.0, -20.0, V, dtype=np.float32)
+        elif kind == "equal":
+            x[b] = np.float32(1.5)
+        else:  # ascending runs of 3000 with a slowly rising base
+            x[b] = (np.arange(V) % 3000).astype(np.float32) * np.float32(1e-3) + np.float32(1e-4) * np.arange(V)
+    p = W.default_params(B)
+    p["temperature"] = rng.uniform(0.5, 1.5, B).astype(np.float32)
+    p["top_k"] = np.array(ks, np.int32)
+    p["top_p"] = 0.95
+    hist, hl = W._hist(rng, B, 64, V)
+    seeds = np.arange(B, dtype=np.uint32) + np.uint32(seed)
+    if bf16:
+        x = W.f32_to_bf16_bits(x)
+    return dict(name=f"order-{kind}-V{V}{'-bf16' if bf16 else ''}", logits=x, bf16=bf16, params=p, hist=hist,
+                hist_len=hl, masks=None, seeds=seeds, u=W.uniforms_for(seeds))
+
+
+@pytest.mark.parametrize("kind", ["ascending", "descending", "equal", "runs"])
+def test_adversarial_orders(ctx, oracle_mod, kind):
+    ks = [1, 2, 64, 300, 1000, 1024]
+    check(ctx, oracle_mod, _order_cfg(kind, W.V_QWEN, ks))
+    check(ctx, oracle_mod, _order_cfg(kind, 40000, ks, seed=12))
+
+
+def test_adversarial_orders_bf16(ctx, oracle_mod):
+    check(ctx, oracle_mod, _order_cfg("ascending", W.V_QWEN, [5, 100, 1024], bf16=True))
