@@ -472,56 +472,61 @@ __device__ __forceinline__ int s_dead_bin(float S) {
     return d > NB - 1 ? NB - 1 : (int)d;
 }
 
-// One full warp advances S over bins [b, bend) whose k-sums (at binade g[b])
+// The whole CTA advances S over bins [b, bend) whose k-sums (at binade g[b])
 // are valid for the current S; stops at the first bin that needs its
 // elements (returned), or at bend. Optionally records S at each bin start.
 // The k-sums are read as the exclusive prefix E = s.ksum over the last pass's
-// bin range (prefix_ksums), so within one binade of S the sum after bin b is
-// m + E[b+1] - E[b0] ulps with no dependence between 32-bin chunks.
-__device__ int warp_walk_bins(float& S, int b, int bend, const Sm& s, const int8_t* g, uint8_t plain_bit,
-                              float stop, bool record) {
-    const int lane = threadIdx.x & 31;
+// bin range (prefix_ksums): within one binade of S the sum after bin b is
+// n = m + E[b+1] - E[b0] ulps (2^23 <= n), and while n <= 2^24 it is the
+// float with exponent e and mantissa n - 2^23 (n = 2^24 gives 2^(e+1)). So
+// every bin is checked at once (thread t takes bins b + t + NT j) and the
+// walk ends at the smallest failing bin. Every thread returns the same b and
+// S. Uses misc->red_i; begins and ends at barriers of all threads.
+__device__ int block_min_int(int v, Misc* m) {
+    v = __reduce_min_sync(FULLMASK, v);
+    if ((threadIdx.x & 31) == 0) m->red_i[threadIdx.x >> 5] = v;
+    __syncthreads();
+    int r = m->red_i[0];
+    for (int q = 1; q < NWARPS; ++q) r = m->red_i[q] < r ? m->red_i[q] : r;
+    __syncthreads();
+    return r;
+}
+__device__ int block_walk_bins(float& S, int b, int bend, const Sm& s, const int8_t* g, uint8_t plain_bit,
+                               float stop, bool record) {
+    Misc* m = s.misc;
+    if (b >= bend) return bend;
     const unsigned long long* E = s.ksum;
     const unsigned long long lim = 1ull << 24;
-    while (b < bend) {
-        if (!(S > 0.0f)) {
-            // an empty bin before the first element leaves S at 0
-            const int bb = b + lane;
-            const bool empty = bb < bend && s.cnt[bb] == 0;
-            const uint32_t em = __ballot_sync(FULLMASK, empty);
-            const int L = (em == FULLMASK) ? 32 : (__ffs(~em) - 1);
-            if (record && lane < L && bb < bend) s.sstart[bb] = S;
-            b += L;
-            if (L < 32) return b < bend ? b : bend;
-            continue;
-        }
-        const int e = binade(S);
-        const float down = pow2f(e - 23);
-        const unsigned long long m = (uint32_t)__fmul_rn(S, pow2f(23 - e));
-        const unsigned long long e0 = E[b];
-        while (b < bend) {
-            const int bb = b + lane;
-            bool ok = false;
-            float before = 0.0f, after = 0.0f;
-            if (bb < bend) {
-                const uint32_t c = s.cnt[bb];
-                const uint8_t f = s.flag[bb];
-                const bool tied = (s.tie[bb >> 5] >> (bb & 31)) & 1u;
-                const bool plain = c == 0 || ((f & plain_bit) && !(f & F_GATH) && g[bb] == e && !tied);
-                const unsigned long long pa = m + (E[bb] - e0), pb = m + (E[bb + 1] - e0);
-                if (pa <= lim) before = __fmul_rn((float)pa, down);
-                if (pb <= lim) after = __fmul_rn((float)pb, down);
-                ok = plain && pa < lim && pb <= lim && !(after >= stop);
-            }
-            const uint32_t okm = __ballot_sync(FULLMASK, ok);
-            const int L = (okm == FULLMASK) ? 32 : (__ffs(~okm) - 1);
-            if (record && lane <= L && bb < bend) s.sstart[bb] = before;
-            if (L > 0) S = __shfl_sync(FULLMASK, after, L - 1);
-            b += L;
-            if (L < 32) return b < bend ? b : bend;
-        }
+    int first = bend;
+    if (!(S > 0.0f)) {
+        // before the first element S stays 0: the walk ends at the first non-empty bin
+        for (int bb = b + threadIdx.x; bb < bend; bb += NT)
+            if (s.cnt[bb] != 0) { first = bb; break; }
+        const int fb = block_min_int(first, m);
+        if (record)
+            for (int bb = b + threadIdx.x; bb < fb; bb += NT) s.sstart[bb] = S;
+        return fb;
     }
-    return bend;
+    const int e = binade(S);
+    const uint32_t ebits = (uint32_t)(e + 127) << 23;
+    const unsigned long long m0 = (uint32_t)__fmul_rn(S, pow2f(23 - e));
+    const unsigned long long e0 = E[b];
+    for (int bb = b + threadIdx.x; bb < bend; bb += NT) {
+        const uint32_t c = s.cnt[bb];
+        const uint8_t f = s.flag[bb];
+        const bool tied = (s.tie[bb >> 5] >> (bb & 31)) & 1u;
+        const bool plain = c == 0 || ((f & plain_bit) && !(f & F_GATH) && g[bb] == e && !tied);
+        const unsigned long long pa = m0 + (E[bb] - e0), pb = m0 + (E[bb + 1] - e0);
+        const float after = __uint_as_float(ebits + (uint32_t)(pb - 0x800000ull));
+        if (!(plain && pa < lim && pb <= lim && !(after >= stop))) { first = bb; break; }
+    }
+    const int fb = block_min_int(first, m);
+    // bins b..fb were reached with the sum in this binade (n <= 2^24)
+    if (record)
+        for (int bb = b + threadIdx.x; bb <= fb && bb < bend; bb += NT)
+            s.sstart[bb] = __uint_as_float(ebits + (uint32_t)(m0 + (E[bb] - e0) - 0x800000ull));
+    if (fb > b) S = __uint_as_float(ebits + (uint32_t)(m0 + (E[fb] - e0) - 0x800000ull));
+    return fb;
 }
 
 // ------------------------------------------------------------ row transform
@@ -1701,56 +1706,60 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 go = false;
                 const int stage = w.stage;
                 if (stage == ST_SWALK) {
-                    if (threadIdx.x < 32) {
-                        float S = w.S;
-                        int b = w.swb;
-                        while (true) {
-                            // bins from `dead` on cannot change S (their largest term is
-                            // below half an ulp of S): the walk ends there
-                            const int dead = S > 0.0f ? s_dead_bin(S) : NB - 1;
-                            b = warp_walk_bins(S, b, dead, s, s.gs, F_PLAINS, POS_INF, true);
-                            if (b >= dead) {
-                                for (int q = b + lane; q < NB - 1; q += 32) s.sstart[q] = S;
-                                b = NB - 1;
-                                break;
-                            }
-                            if (RUNBIN(b)) {
+                    // the bin walk by the whole CTA; a gathered bin's elements by
+                    // warp 0 and a run bin by thread 0, the sum broadcast after
+                    __shared__ float bw_S;
+                    float S = w.S;
+                    int b = w.swb;
+                    while (true) {
+                        // bins from `dead` on cannot change S (their largest term is
+                        // below half an ulp of S): the walk ends there
+                        const int dead = S > 0.0f ? s_dead_bin(S) : NB - 1;
+                        b = block_walk_bins(S, b, dead, s, s.gs, F_PLAINS, POS_INF, true);
+                        if (b >= dead) {
+                            for (int q = b + threadIdx.x; q < NB - 1; q += NT) s.sstart[q] = S;
+                            b = NB - 1;
+                            break;
+                        }
+                        const bool runbin = RUNBIN(b);
+                        if (!runbin && !(s.flag[b] & F_GATH)) break;
+                        if (threadIdx.x < 32) {
+                            if (runbin) {
                                 // one or two runs of equal terms: closed form
                                 if (threadIdx.x == 0) {
                                     s.sstart[b] = S;
                                     const BinRuns R = BIN_RUNS(b);
-                                    
 #pragma unroll
                                     for (int q = 0; q < 2; ++q)
                                         if (q < R.n) qs_run_add(&S, R.t[q], R.c[q], POS_INF);
                                 }
-                                S = __shfl_sync(FULLMASK, S, 0);
-                                ++b;
-                                continue;
-                            }
-                            if (!(s.flag[b] & F_GATH)) break;
-                            const uint32_t off = s.specoff[b];
-                            if (threadIdx.x == 0) s.sstart[b] = S;
-                            warp_walk_terms(S, (int)s.cnt[b], POS_INF, [&](int i) { return s.spect[off + i]; });
-                            ++b;
-                        }
-                        if (threadIdx.x == 0) {
-                            w.S = S;
-                            w.swb = b;
-                            if (b >= NB - 1) {
-                                m->S_n = S;
-                                if (pa) {
-                                    w.stage = ST_CUMPREP;
-                                } else {
-                                    w.stage = ST_DRAW;
-                                    w.cut_all = 1;
-                                    w.n_keep = NSEL;
-                                    w.Sc = S;
-                                    w.mass_cut = 0.0;
-                                }
                             } else {
-                                w.need = b;
+                                const uint32_t off = s.specoff[b];
+                                if (threadIdx.x == 0) s.sstart[b] = S;
+                                warp_walk_terms(S, (int)s.cnt[b], POS_INF, [&](int i) { return s.spect[off + i]; });
                             }
+                            if (threadIdx.x == 0) bw_S = S;
+                        }
+                        __syncthreads();
+                        S = bw_S;
+                        ++b;
+                    }
+                    if (threadIdx.x == 0) {
+                        w.S = S;
+                        w.swb = b;
+                        if (b >= NB - 1) {
+                            m->S_n = S;
+                            if (pa) {
+                                w.stage = ST_CUMPREP;
+                            } else {
+                                w.stage = ST_DRAW;
+                                w.cut_all = 1;
+                                w.n_keep = NSEL;
+                                w.Sc = S;
+                                w.mass_cut = 0.0;
+                            }
+                        } else {
+                            w.need = b;
                         }
                     }
                     __syncthreads();
@@ -1776,16 +1785,21 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     __syncthreads();
                 } else if (stage == ST_CUMWALK) {
                     const float Sn = m->S_n;
-                    if (threadIdx.x < 32) {
-                        float C = w.C;
-                        int b = w.cwb;
-                        int found = -1;
-                        while (true) {
-                            b = warp_walk_bins(C, b, NB - 1, s, s.gc, F_PLAINC, p.top_p, false);
-                            if (b >= NB - 1) break;
-                            const int n = (int)s.cnt[b];
-                            if (RUNBIN(b)) {
-                                int idx = n;
+                    // as the S walk: bins by the whole CTA, elements by warp 0
+                    __shared__ float bw_C;
+                    __shared__ int bw_found;
+                    float C = w.C;
+                    int b = w.cwb;
+                    int found = -1;
+                    while (true) {
+                        b = block_walk_bins(C, b, NB - 1, s, s.gc, F_PLAINC, p.top_p, false);
+                        if (b >= NB - 1) break;
+                        const int n = (int)s.cnt[b];
+                        const bool runbin = RUNBIN(b);
+                        if (!runbin && !(s.flag[b] & F_GATH)) break;
+                        if (threadIdx.x < 32) {
+                            int idx = n;
+                            if (runbin) {
                                 if (threadIdx.x == 0) {
                                     const BinRuns R = BIN_RUNS(b);
                                     long long before = 0;
@@ -1797,18 +1811,22 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                                         before += R.c[q];
                                     }
                                 }
-                                C = __shfl_sync(FULLMASK, C, 0);
-                                idx = __shfl_sync(FULLMASK, idx, 0);
-                                if (idx < n) { found = idx; break; }
-                                ++b;
-                                continue;
+                            } else {
+                                const uint32_t off = s.specoff[b];
+                                idx = warp_walk_terms(C, n, p.top_p, [&](int i) { return __fdiv_rn(s.spect[off + i], Sn); });
                             }
-                            if (!(s.flag[b] & F_GATH)) break;
-                            const uint32_t off = s.specoff[b];
-                            const int idx = warp_walk_terms(C, n, p.top_p, [&](int i) { return __fdiv_rn(s.spect[off + i], Sn); });
-                            if (idx < n) { found = idx; break; }
-                            ++b;
+                            if (threadIdx.x == 0) {
+                                bw_C = C;
+                                bw_found = idx < n ? idx : -1;
+                            }
                         }
+                        __syncthreads();
+                        C = bw_C;
+                        found = bw_found;
+                        if (found >= 0) break;
+                        ++b;
+                    }
+                    if (threadIdx.x < 32) {
                         if (found >= 0) {
                             // S at the cutoff: the S walk's state at the bin start plus the bin's prefix
                             float S = s.sstart[b];
