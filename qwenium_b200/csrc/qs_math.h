@@ -158,11 +158,13 @@ static const double qs_tab_exp64_lo_h[64] = QS_EXP64_LO_TABLE;
 #endif
 
 // ---- expf, as glibc 2.39 computes it --------------------------------------
-QS_HD float qs_expf(float x) {
-    if (x != x) return x + x;                          // NaN
-    if (x == -__builtin_huge_valf()) return 0.0f;
+// qs_expf_tab: the finite x <= 0 part of qs_expf (no NaN, infinity or
+// overflow branches; x below the underflow edge, -inf included, gives 0) with
+// the 2^(i/32) table passed in. Device code keeps a copy of the table in
+// shared memory: lanes index it at random, which a __constant__ array
+// serialises.
+QS_HD float qs_expf_tab(float x, const uint64_t* tab) {
     if (x < -0x1.9fe368p6f) return 0.0f;               // below the smallest subnormal/2
-    if (x > 0x1.62e42ep6f) return __builtin_huge_valf();
     const double InvLn2N = 0x1.71547652b82fep+5;       // 32/ln2
     const double SHIFT = 0x1.8p+52;                    // round-to-integer shift
     const double C0 = 0x1.c6af84b912394p-20;           // cubic for 2^(r/32)
@@ -174,7 +176,7 @@ QS_HD float qs_expf(float x) {
     const uint64_t ki = qs_d2u(kd);
     kd = QS_DSUB(kd, SHIFT);
     const double r = QS_DFMA(InvLn2N, xd, -kd);
-    uint64_t t = QS_TAB_EXP32[ki % 32];
+    uint64_t t = tab[ki % 32];
     t += ki << 47;
     const double s = qs_u2d(t);
     const double zz = QS_DFMA(C0, r, C1);
@@ -183,6 +185,41 @@ QS_HD float qs_expf(float x) {
     y = QS_DFMA(zz, r2, y);
     y = QS_DMUL(y, s);
     return QS_D2F(y);
+}
+QS_HD float qs_expf(float x) {
+    if (x != x) return x + x;                          // NaN
+    if (x == -__builtin_huge_valf()) return 0.0f;
+    if (x > 0x1.62e42ep6f) return __builtin_huge_valf();
+    return qs_expf_tab(x, QS_TAB_EXP32);
+}
+
+// ---- exact scalings of a float, by integer arithmetic ----------------------
+// qs_fixed40(t) = (uint64)(t * 2^40) truncated, for 0 <= t <= 1 (t * 2^40 is
+// exact in double; the conversion truncates).
+QS_HD uint64_t qs_fixed40(float t) {
+    const uint32_t u = qs_f2u(t);
+    const int e = (int)(u >> 23);
+    const uint64_t mt = (uint64_t)((u & 0x7fffffu) | 0x800000u);
+    return e >= 110 ? mt << (e - 110) : (e > 86 ? mt >> (110 - e) : 0u);
+}
+// qs_kround(p, g) = rintf(p * 2^(23-g)) (round half to even) for p >= 0
+// while that is below 2^24; *tie: p * 2^(23-g) is exactly half-way between
+// integers; *big: it is 2^24 or more (the result is then 0).
+QS_HD uint32_t qs_kround(float p, int g, int* tie, int* big) {
+    const uint32_t u = qs_f2u(p);
+    int e = (int)(u >> 23);
+    uint32_t mt = u & 0x7fffffu;
+    if (e) mt |= 0x800000u;
+    else e = 1;                                        // subnormal
+    const int q = e - 127 - g;                         // p * 2^(23-g) = mt * 2^q
+    *tie = 0;
+    *big = q > 0;
+    if (q >= 0) return q > 0 ? 0u : mt;
+    if (q <= -25) return 0u;                           // below 1/2
+    const int sh = -q;
+    const uint32_t fl = mt >> sh, rem = mt & ((1u << sh) - 1u), half = 1u << (sh - 1);
+    *tie = rem == half;
+    return fl + ((rem > half || (rem == half && (fl & 1u))) ? 1u : 0u);
 }
 
 // ---- expm1(z) for 2^-12 <= z <= 19, about 1 ulp (double) ------------------

@@ -72,7 +72,7 @@ struct QsLaunch {
 // Dynamic shared-memory layout; identical on host (sizing) and device.
 struct SmemLayout {
     int off_vals, off_cnt, off_tsum, off_ksum, off_tx, off_sstart, off_flag, off_gs, off_gc, off_tie, off_vmin, off_vmax,
-        off_vcnt, off_spec, off_spect, off_misc, total;
+        off_vcnt, off_spec, off_spect, off_exp, off_misc, total;
 };
 
 // Per-CTA scalars kept at off_misc.
@@ -128,6 +128,7 @@ __host__ __device__ inline SmemLayout smem_layout(int n_s) {
     L.off_vcnt = o;   o = align_up(o + NB * 4, 16);     // counts at vmax (low 16 bits) / vmin (high 16 bits)
     L.off_spec = o;   o = align_up(o + SPEC_CAP * 8, 16);
     L.off_spect = o;  o = align_up(o + SPEC_CAP * 4, 16);
+    L.off_exp = o;    o = align_up(o + 32 * 8, 16);        // expf's 2^(i/32) table
     L.off_misc = o;   o = align_up(o + (int)sizeof(Misc), 16);
     L.total = o;
     return L;

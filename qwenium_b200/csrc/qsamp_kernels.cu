@@ -89,6 +89,7 @@ struct Sm {
     uint32_t* vcnt;            // elements equal to vmax (low 16 bits) / to vmin (high 16 bits)
     unsigned long long* spec;
     float* spect;
+    const uint64_t* exp32;     // qs_expf_tab's table (copied in at kernel start)
     Misc* misc;
 };
 
@@ -155,6 +156,7 @@ __device__ __forceinline__ Sm carve(unsigned char* base, int n_s) {
     s.vcnt = (uint32_t*)(base + L.off_vcnt);
     s.spec = (unsigned long long*)(base + L.off_spec);
     s.spect = (float*)(base + L.off_spect);
+    s.exp32 = (const uint64_t*)(base + L.off_exp);
     s.misc = (Misc*)(base + L.off_misc);
     return s;
 }
@@ -184,8 +186,9 @@ __device__ __forceinline__ bool uniform_bin(const uint32_t* cnt, const uint32_t*
 __device__ __forceinline__ int binof(float x) {
     // x <= 0; larger x -> lower bin. Monotone: rounding of -x*R preserves order.
     // fmaxf maps a NaN x (an infinite logit, outside the contract) to bin 0.
+    // floor(y) for 0 <= y < 2^23: y + 2^23 rounded toward zero is 2^23 + floor(y)
     const float y = fmaxf(__fmul_rn(-x, BIN_R), 0.0f);
-    return y >= (float)(NB - 1) ? NB - 1 : (int)y;
+    return y >= (float)(NB - 1) ? NB - 1 : (int)(__float_as_uint(__fadd_rz(y, 8388608.0f)) - 0x4B000000u);
 }
 
 __device__ __forceinline__ int binade(float s) {  // s > 0, normal
@@ -198,9 +201,6 @@ __device__ __forceinline__ int binade_d(double s) {  // floor(log2 s), s > 0
     return (int)((__double_as_longlong(s) >> 52) & 0x7ff) - 1023;
 }
 
-__device__ __forceinline__ unsigned long long fixed40(float t) {  // t * 2^40, t <= 1
-    return (unsigned long long)__dmul_rn((double)t, 1099511627776.0);
-}
 
 // 64-bit sums from native 32-bit shared-memory atomics (64-bit and float
 // shared atomics are emulated on sm_100 and collapse under contention): the
@@ -1353,7 +1353,8 @@ __device__ void cluster_reduce_bins(cg::cluster_group& cl, const Sm& s, bool cnt
         }
         if (ks && b >= kfrom && b <= kto) {
             unsigned long long k = 0;
-            for (int q = 0; q < CL; ++q) k += ld_u64(peer(cl, s.ksum_lo, q), peer(cl, s.ksum_hi, q), b);
+            for (int q = 0; q < CL; ++q)  // each CTA's limbs: k mod 2^16 sums, k / 2^16 sums
+                k += (unsigned long long)peer(cl, s.ksum_lo, q)[b] + ((unsigned long long)peer(cl, s.ksum_hi, q)[b] << 16);
             peer(cl, s.ksum_lo, 0)[b] = (uint32_t)k;
             peer(cl, s.ksum_hi, 0)[b] = (uint32_t)(k >> 32);
         }
@@ -1613,36 +1614,54 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
             if (rank != 0 && threadIdx.x == 0) m->spec_n = 0;  // this CTA's staged count
             __syncthreads();
             unsigned long long tail_tx = 0ull;
-            const int iters = (r.len + NT - 1) / NT;
+            // two elements per thread per step: their loads, bins and
+            // exponentials are independent (latency is what bounds this loop)
+            const int iters = (r.len + 2 * NT - 1) / (2 * NT);
             for (int it = 0; it < iters; ++it) {
-                const int i = it * NT + threadIdx.x;
-                bool want = false;
-                unsigned long long comp = 0;
-                if (i < r.len) {
-                    const float v = s.vals[i];
-                    if (v != NEG_INF) {
-                        const float x = __fsub_rn(v, M);
-                        const int b = binof(x);
-                        const uint8_t f = s.flag[b];
-                        if (f & F_GATH) { want = true; comp = composite(v, r.lo + i); }
-                        if (b < NB - 1) {
-                            const bool needk = kmode && b >= kfrom && b <= kto && (f & kbit);
-                            if (first || needk) {
-                                const float t = qs_expf(x);
-                                if (first) smem_add_u64(&s.tx_lo[b], &s.tx_hi[b], fixed40(t));
-                                if (needk) {
-                                    const float y = kmode == 1 ? __fmul_rn(t, pow2f(23 - s.gs[b]))
-                                                               : __fmul_rn(__fdiv_rn(t, Sn), pow2f(23 - s.gc[b]));
-                                    if ((y - floorf(y)) == 0.5f) atomicOr(&s.tie[b >> 5], 1u << (b & 31));
-                                    smem_add_u64(&s.ksum_lo[b], &s.ksum_hi[b], (unsigned long long)rintf(y));
+                float vq[2], xq[2];
+                int bq[2];
+                uint8_t fq[2];
+                bool fin[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int i = (2 * it + u) * NT + threadIdx.x;
+                    vq[u] = i < r.len ? s.vals[i] : NEG_INF;
+                    fin[u] = vq[u] != NEG_INF;
+                    xq[u] = __fsub_rn(vq[u], M);
+                    bq[u] = fin[u] ? binof(xq[u]) : NB - 1;
+                    fq[u] = s.flag[bq[u]];
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int b = bq[u];
+                    if (!fin[u]) continue;
+                    if (b < NB - 1) {
+                        const bool needk = kmode && b >= kfrom && b <= kto && (fq[u] & kbit);
+                        if (first || needk) {
+                            const float t = qs_expf_tab(xq[u], s.exp32);
+                            if (first) smem_add_u64(&s.tx_lo[b], &s.tx_hi[b], qs_fixed40(t));
+                            if (needk) {
+                                // k-sums as two u32 limbs (k mod 2^16, k / 2^16): no
+                                // carries, so the adds need no returned value; a
+                                // half-way or >= 2^24 term makes the bin unwalkable
+                                int tie, big;
+                                const uint32_t kk = kmode == 1 ? qs_kround(t, s.gs[b], &tie, &big)
+                                                               : qs_kround(__fdiv_rn(t, Sn), s.gc[b], &tie, &big);
+                                if (tie | big) {
+                                    atomicOr(&s.tie[b >> 5], 1u << (b & 31));
+                                } else {
+                                    atomicAdd(&s.ksum_lo[b], kk & 0xffffu);
+                                    if (kk >> 16) atomicAdd(&s.ksum_hi[b], kk >> 16);
                                 }
                             }
-                        } else if (first) {
-                            tail_tx += fixed40(__expf(x));
                         }
+                    } else if (first) {
+                        tail_tx += qs_fixed40(__expf(xq[u]));
                     }
                 }
-                append_staged(s, want, comp);
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+                    append_staged(s, fin[u] && (fq[u] & F_GATH), composite(vq[u], r.lo + (2 * it + u) * NT + (int)threadIdx.x));
             }
             if (first) {
                 for (int o = 16; o > 0; o >>= 1) tail_tx += __shfl_down_sync(FULLMASK, tail_tx, o);
@@ -1689,7 +1708,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 for (int i = n + threadIdx.x; i < P2; i += NT) s.spec[i] = 0ull;
                 __syncthreads();
                 bitonic_desc(s.spec, P2);
-                for (int i = threadIdx.x; i < n; i += NT) s.spect[i] = qs_expf(__fsub_rn(comp_val(s.spec[i]), M));
+                for (int i = threadIdx.x; i < n; i += NT) s.spect[i] = qs_expf_tab(__fsub_rn(comp_val(s.spec[i]), M), s.exp32);
             }
             __syncthreads();
             if (threadIdx.x == 0) {
@@ -2085,6 +2104,7 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
     const int ncl = gridDim.x / CL;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const Sm s = carve(smem_raw, a.n_s);
+    if (threadIdx.x < 32) ((uint64_t*)s.exp32)[threadIdx.x] = qs_tab_exp32_d[threadIdx.x];
     Misc* m = s.misc;
     const float NEG_INF = -__int_as_float(0x7f800000);
 

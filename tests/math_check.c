@@ -5,6 +5,9 @@
  *   math_check tanh  <part> <nparts>   qs_tanhf == (float)tanhl, x >= +0
  *   math_check tanhx <part> <nparts>   list tanh mismatches as "bits result"
  *   math_check runadd <seed> <cases>    qs_run_add == the sequential float loop
+ *   math_check expftab <part> <nparts>  qs_expf_tab == qs_expf, x in [-104, -0]
+ *   math_check scale <part> <nparts>    qs_fixed40 and qs_kround == their float
+ *                                       definitions, t in [0, 1]
  *
  * Prints "bad=<n>" and exits 0; the driver compares the count.
  */
@@ -36,6 +39,46 @@ int main(int argc, char** argv) {
         }
         /* -inf and the underflow edge */
         if (qs_expf(-INFINITY) != 0.0f) ++bad;
+    } else if (!strcmp(what, "expftab")) {
+        const uint64_t lo = 0x80000000u, hi = 0xC2D00000u; /* -0 .. -104 */
+        const uint64_t n = hi - lo + 1, a = lo + n * part / nparts, b = lo + n * (part + 1) / nparts;
+        for (uint64_t u = a; u < b; ++u) {
+            float x;
+            uint32_t w = (uint32_t)u;
+            memcpy(&x, &w, 4);
+            const float g = qs_expf(x), m = qs_expf_tab(x, qs_tab_exp32_h);
+            if (memcmp(&g, &m, 4)) {
+                if (bad < 5) printf("mismatch x=%a qs_expf=%a tab=%a\n", x, g, m);
+                ++bad;
+            }
+        }
+        if (qs_expf_tab(-INFINITY, qs_tab_exp32_h) != 0.0f) ++bad;
+    } else if (!strcmp(what, "scale")) {
+        static const int gs[] = {-20, -5, 0, 1, 3, 7, 12, 23};
+        const uint64_t lo = 0u, hi = 0x3f800000u; /* +0 .. 1 */
+        const uint64_t n = hi - lo + 1, a = lo + n * part / nparts, b = lo + n * (part + 1) / nparts;
+        for (uint64_t u = a; u < b; ++u) {
+            float t;
+            uint32_t w = (uint32_t)u;
+            memcpy(&t, &w, 4);
+            if ((uint64_t)((double)t * 1099511627776.0) != qs_fixed40(t)) {
+                if (bad < 5) printf("fixed40 mismatch t=%a\n", t);
+                ++bad;
+            }
+            for (int j = 0; j < 8; ++j) {
+                const float y = t * ldexpf(1.0f, 23 - gs[j]);
+                int tie, big;
+                const uint32_t k = qs_kround(t, gs[j], &tie, &big);
+                if (y >= 16777216.0f) {
+                    if (!big) ++bad;
+                    continue;
+                }
+                if (big || k != (uint32_t)rintf(y) || tie != ((y - floorf(y)) == 0.5f)) {
+                    if (bad < 5) printf("kround mismatch t=%a g=%d: %u vs %.1f\n", t, gs[j], k, (double)y);
+                    ++bad;
+                }
+            }
+        }
     } else if (!strcmp(what, "runadd")) {
         /* random runs: S over many binades (mantissas near the binade edge
            too), terms from far below half an ulp up to S, exact ties

@@ -57,3 +57,16 @@ def test_run_add_matches_sequential_float_loop(checker):
     for p in procs:
         out, _ = p.communicate()
         assert p.returncode == 0 and out.strip().endswith("bad=0"), out
+
+
+def test_expf_tab_matches_qs_expf(checker):
+    """qs_expf_tab (the kernels' form: shared-memory table, no special-case
+    branches) equals qs_expf on every float in [-104, 0] and at -inf."""
+    assert _run_parts(checker, "expftab") == 0
+
+
+def test_integer_scalings_match_float_definitions(checker):
+    """qs_fixed40(t) = (uint64)(t * 2^40) and qs_kround(p, g) = rintf(p *
+    2^(23-g)) with its half-way and >= 2^24 flags, on every float in [0, 1]
+    (qs_kround at eight binades)."""
+    assert _run_parts(checker, "scale") == 0
