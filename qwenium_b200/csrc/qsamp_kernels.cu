@@ -2382,24 +2382,34 @@ __device__ unsigned long long block_kth_u64(const unsigned long long* a, int n, 
         }
         __syncthreads();
         if (w == 0) {
-            int acc = 0, found = -1, left = rem, cnt = 0;
-            for (int top = 255; top >= 0 && found < 0; top -= 32) {
-                const int d = top - lane;
-                const int c = (int)hist[d];
-                int pre = c;
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int v = __shfl_up_sync(FULLMASK, pre, o);
-                    if (lane >= o) pre += v;
+            // one scan from the top digit down: lane l holds digits 255 - 8l - j
+            // (j < 8), read as two 16-byte words
+            const uint4 h0 = *(const uint4*)(hist + 248 - 8 * lane);
+            const uint4 h1 = *(const uint4*)(hist + 252 - 8 * lane);
+            const int c[8] = {(int)h1.w, (int)h1.z, (int)h1.y, (int)h1.x, (int)h0.w, (int)h0.z, (int)h0.y, (int)h0.x};
+            int sum = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sum += c[j];
+            int pre = sum;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(FULLMASK, pre, o);
+                if (lane >= o) pre += v;
+            }
+            const uint32_t hm = __ballot_sync(FULLMASK, pre >= rem);
+            int found = -1, left = rem, cnt = 0;
+            if (hm) {
+                const int L = __ffs(hm) - 1;
+                if (lane == L) {
+                    int acc = pre - sum;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (found < 0 && acc + c[j] >= rem) { found = 255 - 8 * L - j; cnt = c[j]; left = rem - acc; }
+                        acc += c[j];
+                    }
                 }
-                const uint32_t hm = __ballot_sync(FULLMASK, acc + pre >= rem);
-                if (hm) {
-                    const int L = __ffs(hm) - 1;
-                    found = top - L;
-                    cnt = __shfl_sync(FULLMASK, c, L);
-                    left = rem - (acc + __shfl_sync(FULLMASK, pre, L) - cnt);
-                } else {
-                    acc += __shfl_sync(FULLMASK, pre, 31);
-                }
+                found = __shfl_sync(FULLMASK, found, L);
+                cnt = __shfl_sync(FULLMASK, cnt, L);
+                left = __shfl_sync(FULLMASK, left, L);
             }
             if (lane == 0) { m->sel_bin = found < 0 ? 0 : found; m->sel_rem = left; m->sel_cnt = cnt; }
         }
