@@ -1326,43 +1326,84 @@ __device__ void cluster_reduce_bins(cg::cluster_group& cl, const Sm& s, bool cnt
     const int rank = cl.block_rank(), CL = cl.num_blocks();
     const int per = NB / CL;
     const int b0 = rank * per;
-    for (int b = b0 + threadIdx.x; b < b0 + per; b += NT) {
-        if (cnt_tsum) {
-            uint32_t c = 0, lo = 0xffffffffu, hi = 0u;
-            unsigned long long t = 0;
+    // one thread per four bins and per kind of sum, 16-byte reads of every
+    // CTA's words (each bin is reduced by the CTA whose slice holds it, so
+    // CTA 0's own partial is read before the same thread overwrites it)
+    const int nq = per / 4;
+    const int nk = ks ? nq : 0, nt = tx ? nq : 0, nc = cnt_tsum ? nq : 0;
+    auto ld4 = [&](const uint32_t* a, int q, int b) { return *(const uint4*)(peer(cl, a, q) + b); };
+    auto st4 = [&](uint32_t* a, int b, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+        *(uint4*)(peer(cl, a, 0) + b) = make_uint4(x, y, z, w);
+    };
+    for (int jq = threadIdx.x; jq < nk + nt + nc; jq += NT) {
+        if (jq < nk) {
+            const int b = b0 + 4 * jq;
+            if (b + 3 < kfrom || b > kto) continue;  // (words outside [kfrom, kto] are not read)
+            unsigned long long k0 = 0, k1 = 0, k2 = 0, k3 = 0;
+            for (int q = 0; q < CL; ++q) {  // each CTA's limbs: k mod 2^16 sums, k / 2^16 sums
+                const uint4 lo = ld4(s.ksum_lo, q, b), hi = ld4(s.ksum_hi, q, b);
+                k0 += (unsigned long long)lo.x + ((unsigned long long)hi.x << 16);
+                k1 += (unsigned long long)lo.y + ((unsigned long long)hi.y << 16);
+                k2 += (unsigned long long)lo.z + ((unsigned long long)hi.z << 16);
+                k3 += (unsigned long long)lo.w + ((unsigned long long)hi.w << 16);
+            }
+            st4(s.ksum_lo, b, (uint32_t)k0, (uint32_t)k1, (uint32_t)k2, (uint32_t)k3);
+            st4(s.ksum_hi, b, (uint32_t)(k0 >> 32), (uint32_t)(k1 >> 32), (uint32_t)(k2 >> 32), (uint32_t)(k3 >> 32));
+        } else if (jq < nk + nt) {
+            const int b = b0 + 4 * (jq - nk);
+            unsigned long long t0 = 0, t1 = 0, t2 = 0, t3 = 0;
             for (int q = 0; q < CL; ++q) {
-                c += peer(cl, s.cnt, q)[b];
-                t += peer(cl, s.tsum32, q)[b];
-                const uint32_t a0 = peer(cl, s.vmin, q)[b], a1 = peer(cl, s.vmax, q)[b];
-                lo = a0 < lo ? a0 : lo;
-                hi = a1 > hi ? a1 : hi;
+                const uint4 lo = ld4(s.tx_lo, q, b), hi = ld4(s.tx_hi, q, b);
+                t0 += (unsigned long long)lo.x | ((unsigned long long)hi.x << 32);
+                t1 += (unsigned long long)lo.y | ((unsigned long long)hi.y << 32);
+                t2 += (unsigned long long)lo.z | ((unsigned long long)hi.z << 32);
+                t3 += (unsigned long long)lo.w | ((unsigned long long)hi.w << 32);
+            }
+            st4(s.tx_lo, b, (uint32_t)t0, (uint32_t)t1, (uint32_t)t2, (uint32_t)t3);
+            st4(s.tx_hi, b, (uint32_t)(t0 >> 32), (uint32_t)(t1 >> 32), (uint32_t)(t2 >> 32), (uint32_t)(t3 >> 32));
+        } else {
+            const int b = b0 + 4 * (jq - nk - nt);
+            uint32_t c[4] = {0u, 0u, 0u, 0u}, lo[4], hi[4];
+            unsigned long long t[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) { lo[e] = 0xffffffffu; hi[e] = 0u; }
+            for (int q = 0; q < CL; ++q) {
+                const uint4 cq = ld4(s.cnt, q, b), tq = ld4(s.tsum32, q, b);
+                const uint4 aq = ld4(s.vmin, q, b), zq = ld4(s.vmax, q, b);
+                const uint32_t cc[4] = {cq.x, cq.y, cq.z, cq.w}, tt[4] = {tq.x, tq.y, tq.z, tq.w};
+                const uint32_t aa[4] = {aq.x, aq.y, aq.z, aq.w}, zz[4] = {zq.x, zq.y, zq.z, zq.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    c[e] += cc[e];
+                    t[e] += tt[e];
+                    lo[e] = aa[e] < lo[e] ? aa[e] : lo[e];
+                    hi[e] = zz[e] > hi[e] ? zz[e] : hi[e];
+                }
             }
             // elements equal to the bin's largest / smallest value, from the
             // CTAs whose own extreme is that value (saturating at 0xffff)
-            uint32_t cmax = 0, cmin = 0;
+            uint32_t cmax[4] = {0u, 0u, 0u, 0u}, cmin[4] = {0u, 0u, 0u, 0u};
             for (int q = 0; q < CL && vcounts; ++q) {
-                const uint32_t a0 = peer(cl, s.vmin, q)[b], a1 = peer(cl, s.vmax, q)[b], vc = peer(cl, s.vcnt, q)[b];
-                if (a1 == hi) cmax += vc & 0xffffu;
-                if (a0 == lo) cmin += a0 == a1 ? (vc & 0xffffu) : (vc >> 16);
+                const uint4 aq = ld4(s.vmin, q, b), zq = ld4(s.vmax, q, b), vq = ld4(s.vcnt, q, b);
+                const uint32_t aa[4] = {aq.x, aq.y, aq.z, aq.w}, zz[4] = {zq.x, zq.y, zq.z, zq.w};
+                const uint32_t vv[4] = {vq.x, vq.y, vq.z, vq.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    if (zz[e] == hi[e]) cmax[e] += vv[e] & 0xffffu;
+                    if (aa[e] == lo[e]) cmin[e] += aa[e] == zz[e] ? (vv[e] & 0xffffu) : (vv[e] >> 16);
+                }
             }
-            peer(cl, s.cnt, 0)[b] = c;
-            peer(cl, s.vmin, 0)[b] = lo;
-            peer(cl, s.vmax, 0)[b] = hi;
-            peer(cl, s.vcnt, 0)[b] = (cmax < 0xffffu ? cmax : 0xffffu) | ((cmin < 0xffffu ? cmin : 0xffffu) << 16);
-            peer(cl, s.tsum, 0)[b] = b < NB - 1 ? (float)((double)t * (double)tsum_scale(b)) : 0.0f;
-        }
-        if (ks && b >= kfrom && b <= kto) {
-            unsigned long long k = 0;
-            for (int q = 0; q < CL; ++q)  // each CTA's limbs: k mod 2^16 sums, k / 2^16 sums
-                k += (unsigned long long)peer(cl, s.ksum_lo, q)[b] + ((unsigned long long)peer(cl, s.ksum_hi, q)[b] << 16);
-            peer(cl, s.ksum_lo, 0)[b] = (uint32_t)k;
-            peer(cl, s.ksum_hi, 0)[b] = (uint32_t)(k >> 32);
-        }
-        if (tx) {
-            unsigned long long t = 0;
-            for (int q = 0; q < CL; ++q) t += ld_u64(peer(cl, s.tx_lo, q), peer(cl, s.tx_hi, q), b);
-            peer(cl, s.tx_lo, 0)[b] = (uint32_t)t;
-            peer(cl, s.tx_hi, 0)[b] = (uint32_t)(t >> 32);
+            uint32_t vc[4], tf[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                vc[e] = (cmax[e] < 0xffffu ? cmax[e] : 0xffffu) | ((cmin[e] < 0xffffu ? cmin[e] : 0xffffu) << 16);
+                tf[e] = __float_as_uint(b + e < NB - 1 ? (float)((double)t[e] * (double)tsum_scale(b + e)) : 0.0f);
+            }
+            st4(s.cnt, b, c[0], c[1], c[2], c[3]);
+            st4(s.vmin, b, lo[0], lo[1], lo[2], lo[3]);
+            st4(s.vmax, b, hi[0], hi[1], hi[2], hi[3]);
+            st4(s.vcnt, b, vc[0], vc[1], vc[2], vc[3]);
+            st4((uint32_t*)s.tsum, b, tf[0], tf[1], tf[2], tf[3]);
         }
     }
     if (ks) {
