@@ -1515,6 +1515,103 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, doub
     __syncthreads();
 }
 
+// The exact part of a pass for one element of bin b (b < NB - 1): t =
+// expf(x), its t sum (first pass) and its integer k-sum term (needk).
+__device__ __forceinline__ void pass_heavy(const Sm& s, float x, int b, bool first, bool needk, int kmode, float Sn) {
+    const float t = qs_expf_tab(x, s.exp32);
+    if (first) smem_add_u64(&s.tx_lo[b], &s.tx_hi[b], qs_fixed40(t));
+    if (needk) {
+        // k-sums as two u32 limbs (k mod 2^16, k / 2^16): no carries, so the
+        // adds need no returned value; a half-way or >= 2^24 term makes the
+        // bin unwalkable
+        int tie, big;
+        const uint32_t kk = kmode == 1 ? qs_kround(t, s.gs[b], &tie, &big)
+                                       : qs_kround(__fdiv_rn(t, Sn), s.gc[b], &tie, &big);
+        if (tie | big) {
+            atomicOr(&s.tie[b >> 5], 1u << (b & 31));
+        } else {
+            atomicAdd(&s.ksum_lo[b], kk & 0xffffu);
+            if (kk >> 16) atomicAdd(&s.ksum_hi[b], kk >> 16);
+        }
+    }
+}
+
+// One pass of a CTA over its slice: the bin of every finite element; the
+// exact t sums (first pass) and integer k-sums of the bins [kfrom, kto] whose
+// flag has the pass's plain bit (kmode 1: S walk at binade gs, kmode 2:
+// top-p walk of t / Sn at binade gc); the elements of gathered bins staged
+// for CTA 0. Elements of the tail bin add approximate t (float sums per
+// thread). The exact part runs with full warps: a warp step where only some
+// lanes need it queues their (x, bin) in the warp's part of spect (free
+// during a pass) and drains 32 entries at a time.
+__device__ __forceinline__ void pass_elements(const RowCtx& r, const Sm& s, float M, bool first, int kmode, int kfrom,
+                                              int kto, float Sn) {
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    const int lane = threadIdx.x & 31;
+    const uint8_t kbit = kmode == 1 ? F_PLAINS : F_PLAINC;
+    float* qx = s.spect + (threadIdx.x >> 5) * 128;        // 64 queued x
+    int* qb = (int*)(s.spect + (threadIdx.x >> 5) * 128 + 64);  // bins (bit 16: needk)
+    int qn = 0;                                               // queued entries (warp-uniform)
+    float tail_f = 0.0f;
+    const int iters = (r.len + 2 * NT - 1) / (2 * NT);
+    for (int it = 0; it < iters; ++it) {
+        float vq[2], xq[2];
+        int bq[2];
+        uint8_t fq[2];
+        bool fin[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int i = (2 * it + u) * NT + threadIdx.x;
+            vq[u] = i < r.len ? s.vals[i] : NEG_INF;
+            fin[u] = vq[u] != NEG_INF;
+            xq[u] = __fsub_rn(vq[u], M);
+            bq[u] = fin[u] ? binof(xq[u]) : NB - 1;
+            fq[u] = s.flag[bq[u]];
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int b = bq[u];
+            const bool body = fin[u] && b < NB - 1;
+            const bool needk = body && kmode && b >= kfrom && b <= kto && (fq[u] & kbit);
+            const bool heavy = body && (first || needk);
+            if (first && fin[u] && b == NB - 1) tail_f += __expf(xq[u]);
+            const uint32_t hm = __ballot_sync(FULLMASK, heavy);
+            if (hm == FULLMASK) {
+                pass_heavy(s, xq[u], b, first, needk, kmode, Sn);
+            } else if (hm) {
+                if (heavy) {
+                    const int pos = qn + __popc(hm & ((1u << lane) - 1u));
+                    qx[pos] = xq[u];
+                    qb[pos] = b | (needk ? 0x10000 : 0);
+                }
+                qn += __popc(hm);
+                if (qn >= 32) {
+                    __syncwarp();
+                    qn -= 32;
+                    const float x = qx[qn + lane];
+                    const int e = qb[qn + lane];
+                    __syncwarp();
+                    pass_heavy(s, x, e & 0xffff, first, (e >> 16) != 0, kmode, Sn);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+            append_staged(s, fin[u] && (fq[u] & F_GATH), composite(vq[u], r.lo + (2 * it + u) * NT + (int)threadIdx.x));
+    }
+    __syncwarp();
+    if (lane < qn) {
+        const int e = qb[lane];
+        pass_heavy(s, qx[lane], e & 0xffff, first, (e >> 16) != 0, kmode, Sn);
+    }
+    if (first) {
+        // the tail's approximate t: float sums per thread, one fixed-point sum per warp
+        unsigned long long tail_tx = qs_fixed40(tail_f);
+        for (int o = 16; o > 0; o >>= 1) tail_tx += __shfl_down_sync(FULLMASK, tail_tx, o);
+        if (lane == 0 && tail_tx) smem_add_u64(&s.tx_lo[NB - 1], &s.tx_hi[NB - 1], tail_tx);
+    }
+}
+
 __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch& a, const Sm& s) {
     Misc* m = s.misc;
     const qsamp_row_params& p = m->prm;
@@ -1646,7 +1743,6 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
             const bool first = m->first_round != 0;
             const int kmode = m->kmode, kfrom = m->kfrom, kto = m->kto;
             const float Sn = m->S_n;
-            const uint8_t kbit = kmode == 1 ? F_PLAINS : F_PLAINC;
             for (int b = threadIdx.x; b < NB; b += NT) {
                 if (kmode && b >= kfrom && b <= kto) { s.ksum_lo[b] = 0u; s.ksum_hi[b] = 0u; }
                 if (first) { s.tx_lo[b] = 0u; s.tx_hi[b] = 0u; }
@@ -1654,60 +1750,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
             for (int q = threadIdx.x; q < NB / 32; q += NT) s.tie[q] = 0u;
             if (rank != 0 && threadIdx.x == 0) m->spec_n = 0;  // this CTA's staged count
             __syncthreads();
-            unsigned long long tail_tx = 0ull;
-            // two elements per thread per step: their loads, bins and
-            // exponentials are independent (latency is what bounds this loop)
-            const int iters = (r.len + 2 * NT - 1) / (2 * NT);
-            for (int it = 0; it < iters; ++it) {
-                float vq[2], xq[2];
-                int bq[2];
-                uint8_t fq[2];
-                bool fin[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int i = (2 * it + u) * NT + threadIdx.x;
-                    vq[u] = i < r.len ? s.vals[i] : NEG_INF;
-                    fin[u] = vq[u] != NEG_INF;
-                    xq[u] = __fsub_rn(vq[u], M);
-                    bq[u] = fin[u] ? binof(xq[u]) : NB - 1;
-                    fq[u] = s.flag[bq[u]];
-                }
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int b = bq[u];
-                    if (!fin[u]) continue;
-                    if (b < NB - 1) {
-                        const bool needk = kmode && b >= kfrom && b <= kto && (fq[u] & kbit);
-                        if (first || needk) {
-                            const float t = qs_expf_tab(xq[u], s.exp32);
-                            if (first) smem_add_u64(&s.tx_lo[b], &s.tx_hi[b], qs_fixed40(t));
-                            if (needk) {
-                                // k-sums as two u32 limbs (k mod 2^16, k / 2^16): no
-                                // carries, so the adds need no returned value; a
-                                // half-way or >= 2^24 term makes the bin unwalkable
-                                int tie, big;
-                                const uint32_t kk = kmode == 1 ? qs_kround(t, s.gs[b], &tie, &big)
-                                                               : qs_kround(__fdiv_rn(t, Sn), s.gc[b], &tie, &big);
-                                if (tie | big) {
-                                    atomicOr(&s.tie[b >> 5], 1u << (b & 31));
-                                } else {
-                                    atomicAdd(&s.ksum_lo[b], kk & 0xffffu);
-                                    if (kk >> 16) atomicAdd(&s.ksum_hi[b], kk >> 16);
-                                }
-                            }
-                        }
-                    } else if (first) {
-                        tail_tx += qs_fixed40(__expf(xq[u]));
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < 2; ++u)
-                    append_staged(s, fin[u] && (fq[u] & F_GATH), composite(vq[u], r.lo + (2 * it + u) * NT + (int)threadIdx.x));
-            }
-            if (first) {
-                for (int o = 16; o > 0; o >>= 1) tail_tx += __shfl_down_sync(FULLMASK, tail_tx, o);
-                if (lane == 0 && tail_tx) smem_add_u64(&s.tx_lo[NB - 1], &s.tx_hi[NB - 1], tail_tx);
-            }
+            pass_elements(r, s, M, first, kmode, kfrom, kto, Sn);
             // the first neg_quota masked ids of the row (they follow every
             // finite logit in the sorted order, by ascending id)
             if (m->neg_quota > 0) {
