@@ -1543,9 +1543,12 @@ __device__ __forceinline__ void pass_heavy(const Sm& s, float x, int b, bool fir
 // for CTA 0. Elements of the tail bin add approximate t (float sums per
 // thread). The exact part runs with full warps: a warp step where only some
 // lanes need it queues their (x, bin) in the warp's part of spect (free
-// during a pass) and drains 32 entries at a time.
+// during a pass) and drains 32 entries at a time. Elements beyond bin bhi
+// (the last bin with work) cost one compare: x below -(bhi + 2) / BIN_R lies
+// in a bin past bhi whatever the rounding of -x * BIN_R, and a warp step
+// whose lanes all hold such elements does nothing else.
 __device__ __forceinline__ void pass_elements(const RowCtx& r, const Sm& s, float M, bool first, int kmode, int kfrom,
-                                              int kto, float Sn) {
+                                              int kto, float Sn, int bhi) {
     const float NEG_INF = -__int_as_float(0x7f800000);
     const int lane = threadIdx.x & 31;
     const uint8_t kbit = kmode == 1 ? F_PLAINS : F_PLAINC;
@@ -1553,6 +1556,7 @@ __device__ __forceinline__ void pass_elements(const RowCtx& r, const Sm& s, floa
     int* qb = (int*)(s.spect + (threadIdx.x >> 5) * 128 + 64);  // bins (bit 16: needk)
     int qn = 0;                                               // queued entries (warp-uniform)
     float tail_f = 0.0f;
+    const float xskip = bhi >= NB - 2 ? NEG_INF : -(float)(bhi + 2) / BIN_R;
     const int iters = (r.len + 2 * NT - 1) / (2 * NT);
     for (int it = 0; it < iters; ++it) {
         float vq[2], xq[2];
@@ -1563,10 +1567,14 @@ __device__ __forceinline__ void pass_elements(const RowCtx& r, const Sm& s, floa
         for (int u = 0; u < 2; ++u) {
             const int i = (2 * it + u) * NT + threadIdx.x;
             vq[u] = i < r.len ? s.vals[i] : NEG_INF;
-            fin[u] = vq[u] != NEG_INF;
             xq[u] = __fsub_rn(vq[u], M);
+            fin[u] = vq[u] != NEG_INF && !(xq[u] < xskip);
+        }
+        if (!__any_sync(FULLMASK, fin[0] || fin[1])) continue;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
             bq[u] = fin[u] ? binof(xq[u]) : NB - 1;
-            fq[u] = s.flag[bq[u]];
+            fq[u] = fin[u] ? s.flag[bq[u]] : (uint8_t)0;
         }
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
@@ -1743,14 +1751,18 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
             const bool first = m->first_round != 0;
             const int kmode = m->kmode, kfrom = m->kfrom, kto = m->kto;
             const float Sn = m->S_n;
+            // the last bin this pass has work in: every bin (first pass: the
+            // t sums), else the k-sum range and the gathered bins
+            int bhi = first ? NB - 1 : (kmode ? kto : -1);
             for (int b = threadIdx.x; b < NB; b += NT) {
                 if (kmode && b >= kfrom && b <= kto) { s.ksum_lo[b] = 0u; s.ksum_hi[b] = 0u; }
                 if (first) { s.tx_lo[b] = 0u; s.tx_hi[b] = 0u; }
+                if ((s.flag[b] & F_GATH) && b > bhi) bhi = b;
             }
             for (int q = threadIdx.x; q < NB / 32; q += NT) s.tie[q] = 0u;
             if (rank != 0 && threadIdx.x == 0) m->spec_n = 0;  // this CTA's staged count
-            __syncthreads();
-            pass_elements(r, s, M, first, kmode, kfrom, kto, Sn);
+            bhi = -block_min_int(-bhi, m);  // (its barriers also complete the stores above)
+            pass_elements(r, s, M, first, kmode, kfrom, kto, Sn, bhi);
             // the first neg_quota masked ids of the row (they follow every
             // finite logit in the sorted order, by ascending id)
             if (m->neg_quota > 0) {
