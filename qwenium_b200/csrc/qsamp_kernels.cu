@@ -1172,6 +1172,7 @@ struct WalkState {
     float draw_prob;
     int drew;
     int need;           // bin to gather next, -1 none
+    int tie_only;       // need stops a walk only for a half-way (or oversized) term
     int dbin;           // bin holding the drawn element
     int big;            // draw by weighted selection instead of gathering
     double acc, tgt;    // survivor mass before dbin, and u * total (probability units)
@@ -1734,6 +1735,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
             w.C = 0.0f;
             w.cut_all = 0;
             w.need = -1;
+            w.tie_only = 0;
         }
         __syncthreads();
         bool ovf = false;
@@ -1759,7 +1761,8 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 if (first) { s.tx_lo[b] = 0u; s.tx_hi[b] = 0u; }
                 if ((s.flag[b] & F_GATH) && b > bhi) bhi = b;
             }
-            for (int q = threadIdx.x; q < NB / 32; q += NT) s.tie[q] = 0u;
+            if (kmode)  // (a pass without k-sums keeps the reduced half-way bits of the last one)
+                for (int q = threadIdx.x; q < NB / 32; q += NT) s.tie[q] = 0u;
             if (rank != 0 && threadIdx.x == 0) m->spec_n = 0;  // this CTA's staged count
             bhi = -block_min_int(-bhi, m);  // (its barriers also complete the stores above)
             pass_elements(r, s, M, first, kmode, kfrom, kto, Sn, bhi);
@@ -1812,6 +1815,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 m->kmode = 0;
                 m->cmd = CMD_DONE;
                 w.need = -1;
+                w.tie_only = 0;
             }
             __syncthreads();
 
@@ -1875,10 +1879,19 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                             }
                         } else {
                             w.need = b;
+                            // a bin whose k-sum is valid at this binade but holds a
+                            // half-way (or oversized) term: walked element by element
+                            w.tie_only = (s.flag[b] & F_PLAINS) && ((s.tie[b >> 5] >> (b & 31)) & 1u) && S > 0.0f &&
+                                         s.gs[b] == binade(S);
                         }
                     }
                     __syncthreads();
-                    if (w.need >= 0) {
+                    if (w.need >= 0 && w.tie_only) {
+                        // gather that bin alone: the later bins' k-sums (and their
+                        // prefix) stay valid, so the pass computes none
+                        if (threadIdx.x == 0) s.flag[w.need] |= F_WANT;
+                        __syncthreads();
+                    } else if (w.need >= 0) {
                         // re-predict the rest from the exact running sum
                         const int fb = w.need;
                         __syncthreads();
@@ -2006,11 +2019,16 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                                 w.stage = ST_DRAW;
                             } else {
                                 w.need = b;
+                                w.tie_only = (s.flag[b] & F_PLAINC) && ((s.tie[b >> 5] >> (b & 31)) & 1u) &&
+                                             C > 0.0f && s.gc[b] == binade(C);
                             }
                         }
                     }
                     __syncthreads();
-                    if (w.need >= 0) {
+                    if (w.need >= 0 && w.tie_only) {
+                        if (threadIdx.x == 0) s.flag[w.need] |= F_WANT;
+                        __syncthreads();
+                    } else if (w.need >= 0) {
                         const int fb = w.need;
                         block_bin_prefix<double>([&](int b) { return b < NB - 1 ? (double)TX(b) * 0x1p-40 : 0.0; },
                                                  s.pref, m, (double*)nullptr);
