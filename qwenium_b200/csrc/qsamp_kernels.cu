@@ -64,7 +64,7 @@ namespace qs {
 #define FULLMASK 0xffffffffu
 
 enum Cmd : int { CMD_DONE = 0, CMD_PASS = 1 };
-enum BinFlag : uint8_t { F_GATH = 1, F_PLAINS = 2, F_PLAINC = 4, F_WANT = 8 };
+enum BinFlag : uint8_t { F_GATH = 1, F_PLAINS = 2, F_PLAINC = 4, F_WANT = 8, F_CROSS = 16 };
 enum Stage : int { ST_SWALK = 0, ST_CUMPREP = 1, ST_CUMWALK = 2, ST_DRAW = 3, ST_FINISH = 4 };
 
 struct Sm {
@@ -1423,6 +1423,28 @@ __device__ void cluster_reduce_bins(cg::cluster_group& cl, const Sm& s, bool cnt
 // float-sum / exact-sum ratio at `from`); bins whose run may leave a binade,
 // and `from` itself, are gathered, the rest get integer sums at the guessed
 // binade.
+// Bins wanted only because the running sum may change binade inside them
+// (F_CROSS) are gathered while their elements total at most CROSS_CAP in bin
+// order; past that they become plain bins at the lower binade (their g is
+// set). A sum that hovers just below a power of two would otherwise want
+// every remaining bin; a plain bin where the binade does change stops the
+// walk (its k-sum leaves the binade), which then gathers that bin alone.
+constexpr uint32_t CROSS_CAP = 1024;
+__device__ void trim_crossings(const Sm& s, uint8_t plain_bit) {
+    uint32_t* pre = (uint32_t*)s.spect;  // (rebuilt by the next pass)
+    block_bin_prefix<uint32_t>([&](int b) { return (s.flag[b] & F_CROSS) ? s.cnt[b] : 0u; }, pre, s.misc,
+                               (uint32_t*)nullptr);
+    for (int b = threadIdx.x; b < NB; b += NT) {
+        uint8_t f = s.flag[b];
+        if (f & F_CROSS) {
+            f = (uint8_t)(f & ~F_CROSS);
+            if (pre[b] + s.cnt[b] > CROSS_CAP) f = (uint8_t)((f & ~F_WANT) | plain_bit);
+            s.flag[b] = f;
+        }
+    }
+    __syncthreads();
+}
+
 __device__ void predict_s(const Sm& s, int from, double ratio) {
     Misc* m = s.misc;
     block_bin_prefix<double>([&](int b) { return b < NB - 1 ? (double)TX(b) * 0x1p-40 : 0.0; }, s.pref, m,
@@ -1432,13 +1454,16 @@ __device__ void predict_s(const Sm& s, int from, double ratio) {
         uint8_t f = (uint8_t)(s.flag[b] & ~(F_PLAINS | F_WANT));
         if (b >= from && b < NB - 1 && s.cnt[b] > 0) {
             const double Pa = s.pref[b] * ratio, Pb = (s.pref[b] + (double)TX(b) * 0x1p-40) * ratio;
-            const bool want = b == from || !(Pa > 0.0) || binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
-            if (want && !RUNBIN(b)) f |= F_WANT;
-            else { f |= F_PLAINS; s.gs[b] = (int8_t)binade_d(Pa > 0.0 ? Pa : 1.0); }
+            const bool must = b == from || !(Pa > 0.0);
+            const bool cross = binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
+            s.gs[b] = (int8_t)binade_d(Pa > 0.0 ? Pa : 1.0);
+            if ((must || cross) && !RUNBIN(b)) f |= must ? F_WANT : (F_WANT | F_CROSS);
+            else f |= F_PLAINS;
         }
         s.flag[b] = f;
     }
     __syncthreads();
+    trim_crossings(s, F_PLAINS);
     if (threadIdx.x == 0) {
         m->kmode = 1;
         m->kfrom = from;
@@ -1488,10 +1513,15 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, doub
             if (b >= from) {
                 if (ca <= pp + 1e-2) {
                     bmax = b > bmax ? b : bmax;
-                    const bool crossing = !(ca > 0) || binade_d(ca * (1 - D)) != binade_d(cb * (1 + D));
+                    const bool must = !(ca > 0) || b == from;
+                    const bool crossing = binade_d(ca * (1 - D)) != binade_d(cb * (1 + D));
                     const bool cut = cb >= pp - Dc && ca <= pp + Dc;
-                    if (((crossing || cut || b == from) && !RUNBIN(b)) || draw) f |= F_WANT;
-                    if (!(f & F_WANT) || RUNBIN(b)) { f |= F_PLAINC; s.gc[b] = (int8_t)binade_d(ca > 0 ? ca : 1.0); }
+                    s.gc[b] = (int8_t)binade_d(ca > 0 ? ca : 1.0);
+                    if (((must || crossing || cut) && !RUNBIN(b)) || draw) {
+                        f |= F_WANT;
+                        if (!must && !cut && !draw) f |= F_CROSS;
+                    }
+                    if (!(f & F_WANT) || RUNBIN(b)) f |= F_PLAINC;
                 }
             } else if (draw) {
                 f |= F_WANT;
@@ -1504,6 +1534,7 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, doub
         bmax = y > bmax ? y : bmax;
     }
     __syncthreads();
+    trim_crossings(s, F_PLAINC);
     if ((threadIdx.x & 31) == 0) m->red_i[threadIdx.x >> 5] = bmax;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1703,24 +1734,26 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 // binade crossings, the top-p cut (none for a uniform bin: its
                 // run is added in closed form) ...
                 bool want = (b == 0) || !(Pa > 0.0);
+                bool cross = false;
                 if (!want) {
                     g = (int8_t)binade_d(Pa);
-                    want = binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
+                    cross = binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
                 }
                 const double ca = Pa / S_est, cb = Pb / S_est;
-                if (RUNBIN(b)) want = false;
+                if (RUNBIN(b)) want = cross = false;
                 // ... and ids: the predicted draw (rows without top-p: the
                 // cumulative pass of a top-p row gathers its own) and the top list
                 const double tgt = u * pp;
                 if (!pa && cb >= tgt - D && ca <= tgt + D) want = true;
                 if ((long long)cpre[b] < topn) want = true;
-                f = want ? F_WANT : F_PLAINS;
+                f = want ? F_WANT : (cross ? (F_WANT | F_CROSS) : F_PLAINS);
             }
             s.flag[b] = f;
             s.gs[b] = g;
             s.gc[b] = 0;
         }
         __syncthreads();
+        trim_crossings(s, F_PLAINS);
         if (threadIdx.x == 0) {
             m->round = 0;
             m->first_round = 1;
