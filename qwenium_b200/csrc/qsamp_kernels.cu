@@ -1172,7 +1172,7 @@ struct WalkState {
     float draw_prob;
     int drew;
     int need;           // bin to gather next, -1 none
-    int tie_only;       // need stops a walk only for a half-way (or oversized) term
+    int tie_only;       // need is gathered alone: a half-way (or oversized) term, or the cut inside
     int dbin;           // bin holding the drawn element
     int big;            // draw by weighted selection instead of gathering
     double acc, tgt;    // survivor mass before dbin, and u * total (probability units)
@@ -1519,7 +1519,7 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, doub
                     s.gc[b] = (int8_t)binade_d(ca > 0 ? ca : 1.0);
                     if (((must || crossing || cut) && !RUNBIN(b)) || draw) {
                         f |= F_WANT;
-                        if (!must && !cut && !draw) f |= F_CROSS;
+                        if (!must && !draw) f |= F_CROSS;  // crossing or cut window: capped
                     }
                     if (!(f & F_WANT) || RUNBIN(b)) f |= F_PLAINC;
                 }
@@ -2052,8 +2052,20 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                                 w.stage = ST_DRAW;
                             } else {
                                 w.need = b;
-                                w.tie_only = (s.flag[b] & F_PLAINC) && ((s.tie[b >> 5] >> (b & 31)) & 1u) &&
-                                             C > 0.0f && s.gc[b] == binade(C);
+                                // a plain bin at the right binade that holds a half-way
+                                // term, or in which the cumulative sum reaches top_p
+                                // (the cut window was capped), is walked element by
+                                // element: the walk ends in it or resumes after it
+                                bool cutin = false;
+                                if ((s.flag[b] & F_PLAINC) && C > 0.0f && s.gc[b] == binade(C)) {
+                                    const int e = binade(C);
+                                    const unsigned long long mC = (uint32_t)__fmul_rn(C, pow2f(23 - e));
+                                    const unsigned long long pb = mC + (s.ksum[b + 1] - s.ksum[b]);
+                                    cutin = pb <= (1ull << 24) &&
+                                            __uint_as_float(((uint32_t)(e + 127) << 23) + (uint32_t)(pb - 0x800000ull)) >= p.top_p;
+                                }
+                                w.tie_only = cutin || ((s.flag[b] & F_PLAINC) && ((s.tie[b >> 5] >> (b & 31)) & 1u) &&
+                                                       C > 0.0f && s.gc[b] == binade(C));
                             }
                         }
                     }
