@@ -561,7 +561,112 @@ __device__ __forceinline__ float post_value(const RowCtx& r, float v) {
     return canon(v);
 }
 
-__device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s) {
+// Penalties over the window (sampling.cpp:124-135 plus the frequency /
+// presence extension): every CTA tables the window ids of its slice with
+// their counts, and the transform gives those ids their penalised values.
+constexpr int PF_SLOTS = 2048;  // penalty hash slots (ids + counts)
+static_assert(2 * PF_SLOTS * 4 <= SPEC_CAP * 8 && HIST_MAX * 4 <= SPEC_CAP * 8,
+              "the penalty window scratch must fit the gather list");
+
+// The window of a row as seen by one CTA: its ids in [r.lo, r.hi) with their
+// counts (an open-addressing hash table of PF_SLOTS ids + counts in the
+// gather list's area, free before the row's passes, for windows of up to
+// 1024 ids; the sorted window for longer ones), and a bit per slice element
+// marking the window ids (pbits, n_s bits). Returns false when the row has
+// no penalties.
+struct PenWin {
+    bool on, sorted, rep_on, fp_on;
+    int w;                   // window length
+    const int32_t* ids;      // sorted window or hash ids
+    const int32_t* cnt;      // hash counts
+};
+__device__ PenWin penalty_table(const RowCtx& r, const QsLaunch& a, const Sm& s, uint32_t* pbits) {
+    const qsamp_row_params& p = *r.p;
+    PenWin pw;
+    pw.rep_on = p.repetition_penalty != 1.0f;
+    pw.fp_on = p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
+    pw.on = false;
+    pw.sorted = false;
+    pw.w = 0;
+    pw.ids = nullptr;
+    pw.cnt = nullptr;
+    if (!(pw.rep_on || pw.fp_on) || !a.hist) return pw;
+    const int len = a.hist_len ? a.hist_len[r.row] : a.hist_stride;
+    if (len <= 0) return pw;
+    const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
+    const int w = (int)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
+    if (w <= 0) return pw;
+    const int32_t* h = a.hist + (size_t)r.row * (size_t)a.hist_stride + (len - w);
+    const bool sorted = w > 1024;
+    int32_t* win = (int32_t*)s.spec;
+    int32_t* ht_id = win;
+    int32_t* ht_cnt = win + PF_SLOTS;
+    for (int q = threadIdx.x; q < (r.len + 31) / 32; q += NT) pbits[q] = 0u;
+    if (sorted) {
+        const int P2 = next_pow2(w);
+        for (int j = threadIdx.x; j < P2; j += NT) win[j] = j < w ? h[j] : 0x7fffffff;
+        __syncthreads();
+        bitonic_asc_i32(win, P2);
+    } else {
+        for (int q = threadIdx.x; q < PF_SLOTS; q += NT) { ht_id[q] = -1; ht_cnt[q] = 0; }
+        __syncthreads();
+    }
+    for (int j = threadIdx.x; j < w; j += NT) {
+        const int32_t id = h[j];
+        if (id < r.lo || id >= r.hi) continue;
+        atomicOr(&pbits[(id - r.lo) >> 5], 1u << ((id - r.lo) & 31));
+        if (sorted) continue;
+        uint32_t slot = ((uint32_t)id * 2654435761u) & (PF_SLOTS - 1);
+        while (true) {  // at most w <= PF_SLOTS / 2 distinct ids: a free slot exists
+            const int old = atomicCAS(&ht_id[slot], -1, id);
+            if (old == -1 || old == id) {
+                atomicAdd(&ht_cnt[slot], 1);
+                break;
+            }
+            slot = (slot + 1) & (PF_SLOTS - 1);
+        }
+    }
+    __syncthreads();
+    pw.on = true;
+    pw.sorted = sorted;
+    pw.w = w;
+    pw.ids = win;
+    pw.cnt = ht_cnt;
+    return pw;
+}
+
+// The value of window id `id` after the penalties (sampling.cpp:124-135 plus
+// the frequency / presence extension): its count from the table.
+__device__ float penalized_value(const RowCtx& r, const PenWin& pw, int id, float raw, uint32_t b16) {
+    const qsamp_row_params& p = *r.p;
+    int c = 0;
+    if (pw.sorted) {
+        int lo = 0, hi = pw.w;  // first position holding id
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (pw.ids[mid] < id) lo = mid + 1;
+            else hi = mid;
+        }
+        while (lo + c < pw.w && pw.ids[lo + c] == id) ++c;
+    } else {
+        uint32_t slot = ((uint32_t)id * 2654435761u) & (PF_SLOTS - 1);
+        while (pw.ids[slot] != id) slot = (slot + 1) & (PF_SLOTS - 1);  // (present: its bit is set)
+        c = pw.cnt[slot];
+    }
+    float v = pre_value(r, id, raw, b16);
+    if (pw.rep_on) v = v < 0.0f ? __fmul_rn(v, p.repetition_penalty) : __fdiv_rn(v, p.repetition_penalty);
+    if (pw.fp_on) {
+        v = __fsub_rn(v, __fmul_rn((float)c, p.frequency_penalty));
+        v = __fsub_rn(v, p.presence_penalty);
+    }
+    return post_value(r, v);
+}
+
+// The slice's values (soft-cap, mask, penalties of the window ids, /T,
+// canon) into shared memory, and this thread's largest value and its id
+// (lowest id among equal values).
+__device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s, const PenWin& pw, const uint32_t* pbits,
+                                float& bm, int& bi) {
     const int tid = threadIdx.x;
     const int ngrp = r.len / 8;
     const bool vec = a.vec_ok && !r.force_on;
@@ -589,6 +694,7 @@ __device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s)
                 for (int e = 0; e < 8; ++e) b16[e] = 0;
             }
             const uint32_t mw = r.mask ? (r.mask[i0 >> 5] >> (i0 & 31)) : 0xffu;
+            const uint32_t pwb = pw.on ? (pbits[(8 * g) >> 5] >> ((8 * g) & 31)) & 0xffu : 0u;
             float o[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
@@ -597,6 +703,14 @@ __device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s)
                 if (!((mw >> e) & 1u)) v = -__int_as_float(0x7f800000);
                 o[e] = post_value(r, v);
             }
+            if (pwb) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    if ((pwb >> e) & 1u) o[e] = penalized_value(r, pw, i0 + e, x[e], b16[e]);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                if (o[e] > bm) { bm = o[e]; bi = i0 + e; }  // ascending ids: strict keeps the lowest
             float4* dst = (float4*)(s.vals + 8 * g);
             dst[0] = make_float4(o[0], o[1], o[2], o[3]);
             dst[1] = make_float4(o[4], o[5], o[6], o[7]);
@@ -604,89 +718,21 @@ __device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s)
         for (int i = r.lo + 8 * ngrp + tid; i < r.hi; i += NT) {
             const float raw = raw_at(r, i);
             const uint32_t b16 = r.dtype == QSAMP_BF16 ? ((const uint16_t*)r.rowp)[i] : 0u;
-            s.vals[i - r.lo] = post_value(r, pre_value(r, i, raw, b16));
+            const bool pen = pw.on && ((pbits[(i - r.lo) >> 5] >> ((i - r.lo) & 31)) & 1u);
+            const float v = pen ? penalized_value(r, pw, i, raw, b16) : post_value(r, pre_value(r, i, raw, b16));
+            s.vals[i - r.lo] = v;
+            if (v > bm || (v == bm && i < bi)) { bm = v; bi = i; }
         }
     } else {
         for (int i = r.lo + tid; i < r.hi; i += NT) {
             const float raw = r.force_on ? 0.0f : raw_at(r, i);
             const uint32_t b16 = (!r.force_on && r.dtype == QSAMP_BF16) ? ((const uint16_t*)r.rowp)[i] : 0u;
-            s.vals[i - r.lo] = post_value(r, pre_value(r, i, raw, b16));
+            const bool pen = pw.on && ((pbits[(i - r.lo) >> 5] >> ((i - r.lo) & 31)) & 1u);
+            const float v = pen ? penalized_value(r, pw, i, raw, b16) : post_value(r, pre_value(r, i, raw, b16));
+            s.vals[i - r.lo] = v;
+            if (v > bm || (v == bm && i < bi)) { bm = v; bi = i; }
         }
     }
-}
-
-// Penalties over the window (sampling.cpp:124-135 plus the frequency /
-// presence extension): every CTA sorts the window ids, and the leader of
-// each run that falls in this slice recomputes its value.
-constexpr int PF_SLOTS = 2048;  // penalty hash slots (ids + counts)
-static_assert(2 * PF_SLOTS * 4 <= SPEC_CAP * 8 && HIST_MAX * 4 <= SPEC_CAP * 8,
-              "the penalty window scratch must fit the gather list");
-
-__device__ void penalty_fixup(const RowCtx& r, const QsLaunch& a, const Sm& s) {
-    const qsamp_row_params& p = *r.p;
-    const bool rep_on = p.repetition_penalty != 1.0f;
-    const bool fp_on = p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
-    if (!(rep_on || fp_on) || !a.hist) return;
-    const int len = a.hist_len ? a.hist_len[r.row] : a.hist_stride;
-    if (len <= 0) return;
-    const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
-    const int w = (int)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
-    if (w <= 0) return;
-    const int start = len - w;
-    const int32_t* h = a.hist + (size_t)r.row * (size_t)a.hist_stride + start;
-    // unique ids of this CTA's range and their counts: an open-addressing
-    // hash table (PF_SLOTS ids + counts in the window area) for windows of
-    // up to 1024 ids, a sort for longer ones
-    const bool sorted = w > 1024;
-    int32_t* win = (int32_t*)s.spec;  // the gather list is free before the row's passes
-    int32_t* ht_id = win;
-    int32_t* ht_cnt = win + PF_SLOTS;
-    if (sorted) {
-        const int P2 = next_pow2(w);
-        for (int j = threadIdx.x; j < P2; j += NT) win[j] = j < w ? h[j] : 0x7fffffff;
-        __syncthreads();
-        bitonic_asc_i32(win, P2);
-    } else {
-        for (int q = threadIdx.x; q < PF_SLOTS; q += NT) { ht_id[q] = -1; ht_cnt[q] = 0; }
-        __syncthreads();
-        for (int j = threadIdx.x; j < w; j += NT) {
-            const int32_t id = h[j];
-            if (id < r.lo || id >= r.hi) continue;
-            uint32_t slot = ((uint32_t)id * 2654435761u) & (PF_SLOTS - 1);
-            while (true) {  // at most w <= PF_SLOTS / 2 distinct ids: a free slot exists
-                const int old = atomicCAS(&ht_id[slot], -1, id);
-                if (old == -1 || old == id) {
-                    atomicAdd(&ht_cnt[slot], 1);
-                    break;
-                }
-                slot = (slot + 1) & (PF_SLOTS - 1);
-            }
-        }
-        __syncthreads();
-    }
-    const int nslots = sorted ? w : PF_SLOTS;
-    for (int j = threadIdx.x; j < nslots; j += NT) {
-        const int32_t id = sorted ? win[j] : ht_id[j];
-        if (id < r.lo || id >= r.hi) continue;
-        int c = 0;
-        if (sorted) {
-            if (j > 0 && win[j - 1] == id) continue;
-            c = 1;
-            while (j + c < w && win[j + c] == id) ++c;
-        } else {
-            c = ht_cnt[j];
-        }
-        const float raw = r.force_on ? 0.0f : raw_at(r, id);
-        const uint32_t b16 = (!r.force_on && r.dtype == QSAMP_BF16) ? ((const uint16_t*)r.rowp)[id] : 0u;
-        float v = pre_value(r, id, raw, b16);
-        if (rep_on) v = v < 0.0f ? __fmul_rn(v, p.repetition_penalty) : __fdiv_rn(v, p.repetition_penalty);
-        if (fp_on) {
-            v = __fsub_rn(v, __fmul_rn((float)c, p.frequency_penalty));
-            v = __fsub_rn(v, p.presence_penalty);
-        }
-        s.vals[id - r.lo] = post_value(r, v);
-    }
-    __syncthreads();
 }
 
 // ------------------------------------------------------------ outputs
@@ -2300,19 +2346,17 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
 
         wait_ready(a, row);
         QS_TMARK(row, 0, rank == 0);
-        transform_slice(r, a, s);
-        __syncthreads();
+        // the window's ids and counts first (bits over the slice in the gs / gc
+        // area, free until the first predictions), then the values with the
+        // penalties and the row max (lowest id among equal maxima, as
+        // std::max_element) in one pass
+        uint32_t* pbits = (uint32_t*)s.gs;
+        const PenWin pw = penalty_table(r, a, s, pbits);
         QS_TMARK(row, 1, rank == 0);
-        penalty_fixup(r, a, s);
-        QS_TMARK(row, 2, rank == 0);
-
-        // row max (lowest id among equal maxima, as std::max_element)
         float bm = NEG_INF;
         int bi = 0x7fffffff;
-        for (int i = threadIdx.x; i < r.len; i += NT) {
-            const float v = s.vals[i];
-            if (v > bm || (v == bm && r.lo + i < bi)) { bm = v; bi = r.lo + i; }
-        }
+        transform_slice(r, a, s, pw, pbits, bm, bi);
+        QS_TMARK(row, 2, rank == 0);
         int bidx;
         bm = block_reduce_max_idx(bm, bi, bidx, m);
         if (threadIdx.x == 0) { m->cmax = bm; m->cmax_idx = bidx; }
