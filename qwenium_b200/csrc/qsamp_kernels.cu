@@ -2547,8 +2547,12 @@ __device__ __forceinline__ unsigned long long block_min_u64(unsigned long long v
 // (candidate keys share their leading bytes), with warp-aggregated histogram
 // updates (lanes with the same digit add once), stopping as soon as the
 // chosen digit's bin holds exactly the remaining rank: the answer is then the
-// smallest key of that bin.
-__device__ unsigned long long block_kth_u64(const unsigned long long* a, int n, int k, uint32_t* hist, Misc* m) {
+// smallest key of that bin. loose > 0: a lower bound of the k-th largest
+// suffices, and the chosen bin's lowest possible key (its prefix, zeros
+// below) is returned as soon as at most `loose` keys of that bin lie below
+// the k-th.
+__device__ unsigned long long block_kth_u64(const unsigned long long* a, int n, int k, uint32_t* hist, Misc* m,
+                                         int loose = 0) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     unsigned long long ka = ~0ull, ko = 0ull;
     for (int i = threadIdx.x; i < n; i += blockDim.x) { ka &= a[i]; ko |= a[i]; }
@@ -2620,6 +2624,10 @@ __device__ unsigned long long block_kth_u64(const unsigned long long* a, int n, 
         prefix |= (unsigned long long)m->sel_bin << shift;
         mask |= 255ull << shift;
         rem = m->sel_rem;
+        if (loose > 0 && m->sel_cnt - rem <= loose && m->sel_cnt != rem) {
+            __syncthreads();  // (sel_* read by every thread before the next caller writes them)
+            return prefix;
+        }
         if (m->sel_cnt == rem) {
             unsigned long long mn = ~0ull;
             for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -2636,8 +2644,9 @@ __device__ unsigned long long block_kth_u64(const unsigned long long* a, int n, 
 // Keep the candidates >= the k-th best (exactly k remain: keys are distinct);
 // returns that key. Survivors are read into registers, then written to the
 // front in any order (the buffer is an unordered set).
-__device__ unsigned long long sn_compact(unsigned long long* cand, int& n, int k, uint32_t* hist, Misc* m) {
-    const unsigned long long ck = block_kth_u64(cand, n, k, hist, m);
+__device__ unsigned long long sn_compact(unsigned long long* cand, int& n, int k, uint32_t* hist, Misc* m,
+                                      int loose = 0) {
+    const unsigned long long ck = block_kth_u64(cand, n, k, hist, m, loose);
     const int lane = threadIdx.x & 31;
     constexpr int J = SN_CAP / SN_NT;
     unsigned long long keep[J];
@@ -2897,8 +2906,10 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
                 // filtered again against the new threshold
                 if (c == 0 || g == SN_G - 1 || c == nchunks - 1) {
                     while (__syncthreads_or(over)) {
+                        // mid-row a lower bound of the k-th best suffices (at most
+                        // SN_SLACK / 2 extra candidates kept); the row's end selects exactly
                         int n = sh_n < cap ? sh_n : cap;
-                        const unsigned long long ck = sn_compact(cand, n, k, hist, m);
+                        const unsigned long long ck = sn_compact(cand, n, k, hist, m, SN_SLACK / 2);
                         if (threadIdx.x == 0) { sh_tau = ck; sh_n = n; sh_xthr = raw_lower_bound(r, comp_val(ck)); }
                         __syncthreads();
                         over = false;
