@@ -308,7 +308,7 @@ qsamp_status qsamp_create(int32_t device, qsamp_ctx** out) {
     cudaSetDevice(device);
     cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
     cudaDeviceGetAttribute(&c->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-    cudaError_t e = c->status.ensure(2);  // [0] status word, [1] row queue
+    cudaError_t e = c->status.ensure(3);  // [0] status word, [1] cluster row queue, [2] stream row queue
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
@@ -393,7 +393,7 @@ static qsamp_status common_setup(qsamp_ctx* c, const qsamp_batch* b, cudaStream_
     }
     s = ensure_luts(c, b, st);
     if (s != QSAMP_OK) return s;
-    if ((e = cudaMemsetAsync(c->status.p, 0, 2 * sizeof(int), st)) != cudaSuccess) return cuda_fail(c, e, "status reset");
+    if ((e = cudaMemsetAsync(c->status.p, 0, 3 * sizeof(int), st)) != cudaSuccess) return cuda_fail(c, e, "status reset");
 
     a = qs::QsLaunch{};
     a.logits = b->logits;
@@ -420,6 +420,7 @@ static qsamp_status common_setup(qsamp_ctx* c, const qsamp_batch* b, cudaStream_
     a.top_cap = b->top_cap;
     a.status = c->status.p;
     a.row_ctr = c->status.p + 1;
+    a.srow_ctr = c->status.p + 2;
     a.max_rounds = kMaxRounds;
     return QSAMP_OK;
 }

@@ -56,6 +56,7 @@ struct QsLaunch {
     const int32_t* rows;           // rows this launch serves, or null: all B rows
     int nrows;                     // entries of rows
     int* row_ctr;                  // row queue of the cluster kernel (zero at launch), or null
+    int* srow_ctr;                 // row queue of the stream kernel (zero at launch), or null
     // vocab-sharded selection: this launch holds logits [v_offset, v_offset + V)
     // of a V_total vocabulary; hist ids and force_token are global ids
     int v_offset;

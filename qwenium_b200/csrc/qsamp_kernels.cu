@@ -2769,7 +2769,10 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
     __shared__ float sh_xthr;  // raw-logit filter derived from sh_tau
     __syncthreads();
 
-    for (int ri = blockIdx.x; ri < a.nrows; ri += gridDim.x) {
+    // CTA b starts with row b; later rows come from a queue (a.srow_ctr, zero
+    // at launch), so that rows of different cost spread over the CTAs
+    __shared__ int sn_next;
+    for (int ri = blockIdx.x; ri < a.nrows;) {
         const int row = a.rows[ri];
         wait_ready(a, row);
         QS_TMARK(row, 0, true);
@@ -3001,6 +3004,9 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
         }
         QS_TMARK(row, 4, true);
         __syncthreads();
+        if (threadIdx.x == 0) sn_next = a.srow_ctr ? (int)gridDim.x + atomicAdd(a.srow_ctr, 1) : ri + (int)gridDim.x;
+        __syncthreads();
+        ri = sn_next;
     }
 }
 
