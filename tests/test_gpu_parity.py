@@ -206,3 +206,13 @@ def test_adversarial_orders(ctx, oracle_mod, kind):
 
 def test_adversarial_orders_bf16(ctx, oracle_mod):
     check(ctx, oracle_mod, _order_cfg("ascending", W.V_QWEN, [5, 100, 1024], bf16=True))
+
+
+@pytest.mark.parametrize("seed", [1000, 2000, 6000])
+def test_config2_bench_batches(ctx, oracle_mod, seed):
+    """Whole B=256 config2 batches of the bench's seeds: rows whose running sum
+    hovers just below a power of two (seed 2000, row 189: the capped crossing
+    window), deep top-p cuts inside large bins (seed 6000, row 214; seed 1000,
+    row 91) and walks stopped by half-way terms (tie-only gathers) are all in
+    them."""
+    check(ctx, oracle_mod, W.config2(seed, B=256))
