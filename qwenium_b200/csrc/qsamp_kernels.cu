@@ -372,11 +372,55 @@ __device__ void bitonic_desc_reg(unsigned long long* a, int n) {
     __syncthreads();
 }
 
+// One warp sorts 32 E keys held in registers (key lane * E + e), descending:
+// the bitonic network fully unrolled, partners at distance >= E through
+// shuffles, the rest inside the lane.
+template <int E>
+__device__ __forceinline__ void warp_sort_desc(unsigned long long* a) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = a[lane * E + e];
+#pragma unroll
+    for (int k = 2; k <= 32 * E; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= E) {
+                // k > j >= E: the key index bits k and j are the lane's
+                const bool desc = ((lane * E) & k) == 0;
+                const bool keep_max = (((lane * E) & j) == 0) == desc;
+#pragma unroll
+                for (int e = 0; e < E; ++e) v[e] = keep_of(v[e], __shfl_xor_sync(FULLMASK, v[e], j / E), keep_max);
+            } else {
+#pragma unroll
+                for (int e = 0; e < E; ++e) {
+                    if ((e & j) == 0) {
+                        const bool desc = ((lane * E + e) & k) == 0;
+                        const unsigned long long x = v[e], y = v[e | j];
+                        if (desc ? (x < y) : (x > y)) { v[e] = y; v[e | j] = x; }
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) a[lane * E + e] = v[e];
+}
+
 // Entries [n, next power of two) must hold 0 (the smallest key); n <= 4096.
+// Up to 128 keys one warp sorts them in registers (no barriers inside the
+// network); above, E keys per thread with shared-memory exchanges.
 __device__ void bitonic_desc(unsigned long long* a, int n) {
-    if (n < 32) {
-        for (int i = n + threadIdx.x; i < 32; i += blockDim.x) a[i] = 0ull;
-        n = 32;
+    if (n <= 128) {
+        if (threadIdx.x < 32) {
+            for (int i = n + threadIdx.x; i < 32; i += 32) a[i] = 0ull;
+            __syncwarp();
+            if (n <= 32) warp_sort_desc<1>(a);
+            else if (n <= 64) warp_sort_desc<2>(a);
+            else warp_sort_desc<4>(a);
+        }
+        __syncthreads();
+        return;
     }
     if (n >= 8 * NT) bitonic_desc_reg<8>(a, n);
     else if (n >= 4 * NT) bitonic_desc_reg<4>(a, n);
