@@ -408,16 +408,19 @@ __device__ __forceinline__ void warp_sort_desc(unsigned long long* a) {
 }
 
 // Entries [n, next power of two) must hold 0 (the smallest key); n <= 4096.
-// Up to 128 keys one warp sorts them in registers (no barriers inside the
-// network); above, E keys per thread with shared-memory exchanges.
+// Up to WMAX keys (128, or 256 where the registers allow) one warp sorts them
+// in registers (no barriers inside the network); above, E keys per thread
+// with shared-memory exchanges.
+template <int WMAX = 128>
 __device__ void bitonic_desc(unsigned long long* a, int n) {
-    if (n <= 128) {
+    if (n <= WMAX) {
         if (threadIdx.x < 32) {
             for (int i = n + threadIdx.x; i < 32; i += 32) a[i] = 0ull;
             __syncwarp();
             if (n <= 32) warp_sort_desc<1>(a);
             else if (n <= 64) warp_sort_desc<2>(a);
-            else warp_sort_desc<4>(a);
+            else if (WMAX < 256 || n <= 128) warp_sort_desc<4>(a);
+            else warp_sort_desc<(WMAX >= 256 ? 8 : 4)>(a);
         }
         __syncthreads();
         return;
@@ -1929,7 +1932,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 const int P2 = next_pow2(n > 1 ? n : 1);
                 for (int i = n + threadIdx.x; i < P2; i += NT) s.spec[i] = 0ull;
                 __syncthreads();
-                bitonic_desc(s.spec, P2);
+                bitonic_desc<256>(s.spec, P2);
                 for (int i = threadIdx.x; i < n; i += NT) s.spect[i] = qs_expf_tab(__fsub_rn(comp_val(s.spec[i]), M), s.exp32);
             }
             __syncthreads();
