@@ -2538,22 +2538,24 @@ __device__ void finish_sorted(const QsLaunch& a, int row, int k, const unsigned 
 
 // ============================================================ streaming kernel
 // Greedy rows and top-k rows (k <= KMAX) with a short penalty window: one CTA
-// per row, the row streamed from HBM once in 2048-element chunks, two CTAs per
+// per row, the row streamed from HBM once in 4096-element chunks, two CTAs per
 // SM. Top-k keeps a candidate buffer under an exact threshold: an element
 // enters iff its (value, -id) composite beats the k-th best composite of the
 // last compaction, so the final top-k (value desc, id asc) is always among the
 // kept ones. The threshold is also carried back to the raw logit (the row
 // transform is monotone), so most elements cost one compare.
 constexpr int SN_NT = 512;
-constexpr int SN_CH = 2048;                // elements per chunk
+constexpr int SN_CH = 4096;                // elements per chunk
 constexpr int SN_PER = SN_CH / SN_NT;      // consecutive elements per thread per chunk
-constexpr int SN_CAP = KMAX + 2 * SN_CH;   // candidate buffer entries
+constexpr int SN_CAP = KMAX + 4096;        // candidate buffer entries
 constexpr int SN_SLACK = 256;              // compaction once k + SN_SLACK are held
 constexpr int SN_HMAX = 1024;              // penalty window this kernel takes
 constexpr int SN_HT = 2 * SN_HMAX;         // window hash table slots (power of two)
 constexpr int SN_G = 4;                    // chunks per super-chunk (one barrier each)
-static_assert(SN_PER == 4 && SN_G * SN_PER <= 32 && SN_CAP % SN_NT == 0, "stream kernel shape");
-static_assert(KMAX + SN_SLACK + SN_CH + SN_HMAX <= SN_CAP, "candidate buffer bound");
+static_assert(SN_PER == 8 && SN_G * SN_PER <= 32 && SN_CAP % SN_NT == 0, "stream kernel shape");
+// appends past SN_CAP - SN_HMAX wait for a compaction, which the trigger
+// (at most SN_CAP - SN_HMAX - 512 held) requests first
+static_assert(KMAX + SN_SLACK <= SN_CAP - SN_HMAX - 512, "candidate buffer bound");
 
 struct SnLayout {
     int off_cand, off_hist, off_uid, off_ucnt, off_tail, off_bitmap, off_misc, total;
@@ -2749,13 +2751,18 @@ __device__ __forceinline__ void sn_load(const RowCtx& r, bool vec, int i0, int V
                                         uint32_t (&b)[SN_PER]) {
     if (vec && i0 + SN_PER <= V) {
         if (r.dtype == QSAMP_BF16) {
-            const uint2 q = __ldg((const uint2*)((const uint16_t*)r.rowp + i0));
-            b[0] = q.x & 0xffffu; b[1] = q.x >> 16; b[2] = q.y & 0xffffu; b[3] = q.y >> 16;
+            const uint4 q = __ldg((const uint4*)((const uint16_t*)r.rowp + i0));
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-            for (int e = 0; e < SN_PER; ++e) x[e] = __uint_as_float(b[e] << 16);
+            for (int e = 0; e < SN_PER; ++e) {
+                b[e] = (w[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+                x[e] = __uint_as_float(b[e] << 16);
+            }
         } else {
-            const float4 q = __ldg((const float4*)((const float*)r.rowp + i0));
-            x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+            const float4 q0 = __ldg((const float4*)((const float*)r.rowp + i0));
+            const float4 q1 = __ldg((const float4*)((const float*)r.rowp + i0 + 4));
+            x[0] = q0.x; x[1] = q0.y; x[2] = q0.z; x[3] = q0.w;
+            x[4] = q1.x; x[5] = q1.y; x[6] = q1.z; x[7] = q1.w;
 #pragma unroll
             for (int e = 0; e < SN_PER; ++e) b[e] = 0u;
         }
@@ -2893,7 +2900,7 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
         int bi = 0x7fffffff;
         const bool vec = a.vec_ok != 0;  // 16-byte aligned rows
         const int nchunks = (V + SN_CH - 1) / SN_CH;
-        const int trig = min(k + SN_SLACK, SN_CAP - SN_CH);
+        const int trig = min(k + SN_SLACK, SN_CAP - SN_HMAX - 512);
         const int cap = SN_CAP - SN_HMAX;  // streamed candidates (the window's ids follow)
         bool over = false;                 // since the last barrier the list passed trig
         uint32_t pend = 0u;                // passing elements of this super-chunk that found the list full
@@ -2940,8 +2947,11 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
                         if (lm) {
                             e = __ffs((int)lm) - 1;
                             lm &= lm - 1u;
-                            const float xv = e == 0 ? x[0] : (e == 1 ? x[1] : (e == 2 ? x[2] : x[3]));
-                            const uint32_t hv = e == 0 ? b16[0] : (e == 1 ? b16[1] : (e == 2 ? b16[2] : b16[3]));
+                            float xv = x[0];
+                            uint32_t hv = b16[0];
+#pragma unroll
+                            for (int q = 1; q < SN_PER; ++q)
+                                if (e == q) { xv = x[q]; hv = b16[q]; }
                             const float v = post_value(r, pre_value(r, i0 + e, xv, hv));
                             cc = composite(v, i0 + e);
                             ok = cc > tau;
