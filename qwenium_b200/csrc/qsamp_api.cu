@@ -153,9 +153,9 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, Plan& out) {
         if (e != cudaSuccess) return cuda_fail(c, e, "cudaFuncSetAttribute");
         c->attrs_smem = c->max_dyn;
     }
-    const int sizes[5] = {1, 2, 4, 8, 16};
+    const int sizes[6] = {1, 2, 4, 6, 8, 16};
     int first = -1;
-    for (int i = 0; i < 5; ++i) {
+    for (int i = 0; i < 6; ++i) {
         const int n_s = qs::align_up((V + sizes[i] - 1) / sizes[i], 8);
         if ((size_t)qs::smem_layout(n_s).total <= c->max_dyn) {
             first = i;
@@ -166,7 +166,7 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, Plan& out) {
         return fail(c, QSAMP_ERR_UNSUPPORTED, "V=%d exceeds the largest vocabulary one 16-CTA cluster holds (%d)", V,
                     16 * (int)((c->max_dyn - (size_t)qs::smem_layout(0).total) / 4 / 8 * 8));
     int pick = first;
-    for (int i = first; i < 5; ++i) {
+    for (int i = first; i < 6; ++i) {
         const int cl = sizes[i];
         const int n_s = qs::align_up((V + cl - 1) / cl, 8);
         const size_t smem = (size_t)qs::smem_layout(n_s).total;
@@ -506,6 +506,16 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         Plan plan;
         s = plan_for(c, n_cluster, b->V, plan);
         if (s != QSAMP_OK) return s;
+        if (n_stream > 0) {
+            // the SMs split by the rows' expected work (measured on B200, V=151936):
+            // a stream row takes about 48 SM-us (half an SM for ~95 us), a
+            // cluster row about 140 us on each of its CTAs' SMs; clusters leave
+            // the stream kernel its share
+            const double ws = 48.0 * n_stream, wc = 140.0 * plan.cl * n_cluster;
+            const int reserve = (int)std::ceil(c->num_sms * ws / (ws + wc));
+            const int cap = (c->num_sms - reserve) / plan.cl;
+            plan.clusters = std::max(1, std::min(plan.clusters, cap));
+        }
         qs::QsLaunch ca = a;
         ca.rows = c->rows.p + n_stream;
         ca.nrows = n_cluster;

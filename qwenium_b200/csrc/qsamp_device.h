@@ -15,7 +15,7 @@ constexpr int NWARPS = NT / 32;
 constexpr int NB = 2048;           // value bins over x = l - max (bin NB-1 = tail)
 constexpr float BIN_R = 112.0f;    // bins per nat: bin(x) = min(NB-1, (int)(-x * BIN_R))
 constexpr int HIST_MAX = 4096;     // longest penalty window handled on the device
-constexpr int SPEC_CAP = 4096;     // elements gathered in sorted order per round
+constexpr int SPEC_CAP = 2048;     // elements gathered in sorted order per round
 constexpr int KMAX = 1024;         // largest top-k served by the sorted-candidate path
 constexpr int MAX_LUT = 4;         // distinct soft-cap values per call with bf16 tables
 constexpr int MAX_CLUSTER = 16;

@@ -1418,8 +1418,10 @@ __device__ void leader_weighted_select(cg::cluster_group& cl, const Sm& s, int n
 __device__ void cluster_reduce_bins(cg::cluster_group& cl, const Sm& s, bool cnt_tsum, bool ks, int kfrom, int kto,
                                     bool tx, bool vcounts = false) {
     const int rank = cl.block_rank(), CL = cl.num_blocks();
-    const int per = NB / CL;
-    const int b0 = rank * per;
+    // CTA r reduces bins [b0, b1): whole 32-bin words (any cluster size)
+    const int span = ((NB + CL - 1) / CL + 31) & ~31;
+    const int b0 = min(NB, rank * span), b1 = min(NB, b0 + span);
+    const int per = b1 - b0;
     // one thread per four bins and per kind of sum, 16-byte reads of every
     // CTA's words (each bin is reduced by the CTA whose slice holds it, so
     // CTA 0's own partial is read before the same thread overwrites it)
