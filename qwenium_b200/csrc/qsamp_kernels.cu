@@ -33,7 +33,7 @@ namespace cg = cooperative_groups;
 // row's leading CTA records %globaltimer into qs_phase[row][slot]. Expands to
 // nothing in the shipped library.
 #ifdef QS_PHASE_TIMING
-__device__ unsigned long long qs_phase[8192][24];
+__device__ unsigned long long qs_phase[8192][40];
 #define QS_TMARK(row, slot, lead)                                                 \
     do {                                                                         \
         if (threadIdx.x == 0 && (lead) && (row) < 8192) {                        \
@@ -47,15 +47,25 @@ __device__ unsigned long long qs_phase[8192][24];
     do {                          \
     } while (0)
 #endif
+// Sub-phase cycle counts (profiling builds): QS_SUB(row, j, lead) adds the
+// clock64 cycles since the previous QS_SUB (or QS_SUB_BEGIN) of this thread to
+// qs_phase[row][24 + j].
 #ifdef QS_PHASE_TIMING
-#define QS_CYC(var) long long var = clock64()
-#define QS_ACC(acc, from) acc += clock64() - from
-#else
-#define QS_CYC(var) \
-    do {            \
+#define QS_SUB_BEGIN() long long qs_sub_t = clock64()
+#define QS_SUB(row, j, lead)                                                     \
+    do {                                                                         \
+        if (threadIdx.x == 0 && (lead) && (row) < 8192) {                        \
+            const long long t_ = clock64();                                      \
+            qs_phase[(row)][24 + (j)] += (unsigned long long)(t_ - qs_sub_t);    \
+            qs_sub_t = t_;                                                       \
+        }                                                                        \
     } while (0)
-#define QS_ACC(acc, from) \
-    do {                  \
+#else
+#define QS_SUB_BEGIN() \
+    do {               \
+    } while (0)
+#define QS_SUB(row, j, lead) \
+    do {                     \
     } while (0)
 #endif
 
@@ -712,8 +722,10 @@ __device__ float penalized_value(const RowCtx& r, const PenWin& pw, int id, floa
 // The slice's values (soft-cap, mask, penalties of the window ids, /T,
 // canon) into shared memory, and this thread's largest value and its id
 // (lowest id among equal values).
+// insm: the fp32 slice is already in s.vals (bulk copy of its first
+// 4 * floor(len / 4) logits); the groups of 8 are transformed in place.
 __device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s, const PenWin& pw, const uint32_t* pbits,
-                                float& bm, int& bi) {
+                                float& bm, int& bi, bool insm) {
     const int tid = threadIdx.x;
     const int ngrp = r.len / 8;
     const bool vec = a.vec_ok && !r.force_on;
@@ -732,6 +744,13 @@ __device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s,
                 }
 #pragma unroll
                 for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(b16[e] << 16);
+            } else if (insm) {
+                const float4 p0 = ((const float4*)(s.vals + 8 * g))[0];
+                const float4 p1 = ((const float4*)(s.vals + 8 * g))[1];
+                x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
+                x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) b16[e] = 0;
             } else {
                 const float4 p0 = __ldg((const float4*)((const float*)r.rowp + i0));
                 const float4 p1 = __ldg((const float4*)((const float*)r.rowp + i0 + 4));
@@ -788,6 +807,45 @@ __device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s,
 // backs off; the wait is bounded (about 3 s), after which the status reports
 // DEV_TIMEOUT and the row is processed anyway. Every thread of the CTA must
 // call it (it ends with a block barrier).
+// A CTA's fp32 slice comes into shared memory by bulk copies (cp.async.bulk,
+// no multicast) that complete on an mbarrier: one thread issues them, the
+// transform then works in place. The barrier is initialised once per CTA and
+// used once per row (phase parity flips per use).
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void slice_bar_init(uint64_t* bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(bar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// Thread 0 only: bytes (a multiple of 16, src and dst 16-byte aligned) in
+// pieces of at most 32 KB.
+__device__ __forceinline__ void slice_bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+    for (uint32_t off = 0; off < bytes; off += 32768u) {
+        const uint32_t n = bytes - off < 32768u ? bytes - off : 32768u;
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         smem_addr((char*)dst + off)),
+                     "l"((const char*)src + off), "r"(n), "r"(smem_addr(bar))
+                     : "memory");
+    }
+}
+// Waits for the phase with the given parity; false after about one second.
+__device__ bool slice_bar_wait(uint64_t* bar, uint32_t parity) {
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    while (true) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_addr(bar)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > 1000000000ull) return false;
+    }
+}
+
 __device__ void wait_ready(const QsLaunch& a, int row) {
     if (!a.ready) return;
     if (threadIdx.x == 0) {
@@ -1922,6 +1980,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
         }
         if (it_no < 5) QS_TMARK(r.row, 9 + 3 * it_no, rank == 0);
         if (rank == 0) {
+            QS_SUB_BEGIN();
             if (m->kmode) {
                 // the walks read the pass's k-sums as an exclusive prefix over its range
                 const int kf = m->kfrom, kt = m->kto;
@@ -1929,6 +1988,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     [&](int b) { return (b >= kf && b <= kt) ? KSUM(b) : 0ull; }, s.ksum, m,
                     (unsigned long long*)nullptr);
             }
+            QS_SUB(r.row, 0, true);
             {
                 const int n = m->spec_n < SPEC_CAP ? m->spec_n : SPEC_CAP;
                 const int P2 = next_pow2(n > 1 ? n : 1);
@@ -1946,6 +2006,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 w.tie_only = 0;
             }
             __syncthreads();
+            QS_SUB(r.row, 1, true);
 
             // ---- walk state machine: runs until it needs a pass or is done
             bool go = true;
@@ -2014,6 +2075,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         }
                     }
                     __syncthreads();
+                    QS_SUB(r.row, 2, true);
                     if (w.need >= 0 && w.tie_only) {
                         // gather that bin alone: the later bins' k-sums (and their
                         // prefix) stay valid, so the pass computes none
@@ -2032,6 +2094,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     } else {
                         go = true;
                     }
+                    QS_SUB(r.row, 3, true);
                 } else if (stage == ST_CUMPREP) {
                     predict_c(s, 0, 1.0, p.top_p, row_u(a, r.row, p));
                     if (threadIdx.x == 0) {
@@ -2039,6 +2102,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         w.need = 0;  // a pass (bin 0 is gathered again)
                     }
                     __syncthreads();
+                    QS_SUB(r.row, 4, true);
                 } else if (stage == ST_CUMWALK) {
                     const float Sn = m->S_n;
                     // as the S walk: bins by the whole CTA, elements by warp 0
@@ -2165,6 +2229,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         }
                     }
                     __syncthreads();
+                    QS_SUB(r.row, 5, true);
                     if (w.need >= 0 && w.tie_only) {
                         if (threadIdx.x == 0) s.flag[w.need] |= F_WANT;
                         __syncthreads();
@@ -2186,6 +2251,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         }
                         go = true;
                     }
+                    QS_SUB(r.row, 6, true);
                 } else if (stage == ST_DRAW) {
                     // Survivors: ranks [0, n_keep), probabilities p_i = t_i / Sc.
                     // Whole bins below the cutoff bin count by their t sums,
@@ -2292,6 +2358,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         if (threadIdx.x == 0) m->kmode = 0;
                         __syncthreads();
                     }
+                    QS_SUB(r.row, 7, true);
                 } else if (stage == ST_FINISH) {
                     if (threadIdx.x == 0) {
                         qsamp_row_result res;
@@ -2316,6 +2383,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                         }
                     }
                     __syncthreads();
+                    QS_SUB(r.row, 8, true);
                 }
             }
             if (w.need >= 0) {
@@ -2338,6 +2406,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     __syncthreads();
                 }
             }
+            QS_SUB(r.row, 9, true);
             if (it_no < 5) QS_TMARK(r.row, 10 + 3 * it_no, true);
         }
         ++it_no;
@@ -2361,6 +2430,10 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
     if (threadIdx.x < 32) ((uint64_t*)s.exp32)[threadIdx.x] = qs_tab_exp32_d[threadIdx.x];
     Misc* m = s.misc;
     const float NEG_INF = -__int_as_float(0x7f800000);
+    __shared__ __align__(8) uint64_t slice_bar;
+    uint32_t slice_par = 0;
+    if (threadIdx.x == 0) slice_bar_init(&slice_bar);
+    __syncthreads();
 
     const int nrows = a.rows ? a.nrows : a.B;
     // cluster c starts with row c; later rows come from a queue (a.row_ctr,
@@ -2394,6 +2467,10 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
         }
 
         wait_ready(a, row);
+        // fp32 slices: the bulk copy runs while the penalty table is built
+        const bool insm = a.dtype != QSAMP_BF16 && a.vec_ok && !r.force_on && r.len >= 8;
+        if (insm && threadIdx.x == 0)
+            slice_bulk_load(s.vals, (const float*)r.rowp + r.lo, (uint32_t)(r.len / 4) * 16u, &slice_bar);
         QS_TMARK(row, 0, rank == 0);
         // the window's ids and counts first (bits over the slice in the gs / gc
         // area, free until the first predictions), then the values with the
@@ -2402,9 +2479,19 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
         uint32_t* pbits = (uint32_t*)s.gs;
         const PenWin pw = penalty_table(r, a, s, pbits);
         QS_TMARK(row, 1, rank == 0);
+        if (insm) {
+            if (!slice_bar_wait(&slice_bar, slice_par)) {
+                // (not expected: the copy reads this row's own bytes) report it,
+                // and wait once more so that no copy is still in flight
+                if (threadIdx.x == 0) set_status(a.status, DEV_TIMEOUT);
+                slice_bar_wait(&slice_bar, slice_par);
+            }
+            slice_par ^= 1u;
+        }
+        QS_TMARK(row, 34, rank == 0);
         float bm = NEG_INF;
         int bi = 0x7fffffff;
-        transform_slice(r, a, s, pw, pbits, bm, bi);
+        transform_slice(r, a, s, pw, pbits, bm, bi, insm);
         QS_TMARK(row, 2, rank == 0);
         int bidx;
         bm = block_reduce_max_idx(bm, bi, bidx, m);
@@ -3427,7 +3514,7 @@ extern "C" cudaError_t qs_launch_stream(const qs::QsLaunch* a, int grid, size_t 
 #ifdef QS_PHASE_TIMING
 extern "C" cudaError_t qs_phase_read(void* host) { return cudaMemcpyFromSymbol(host, qs_phase, sizeof(qs_phase)); }
 extern "C" cudaError_t qs_phase_clear() {
-    static unsigned long long z[8192][24];
+    static unsigned long long z[8192][40];
     return cudaMemcpyToSymbol(qs_phase, z, sizeof(z));
 }
 #endif
