@@ -143,7 +143,7 @@ void t_end(qsamp_ctx* c, int k, cudaStream_t st) {
     }
 }
 
-qsamp_status plan_for(qsamp_ctx* c, int B, int V, Plan& out) {
+qsamp_status plan_for(qsamp_ctx* c, int B, int V, bool vcounts, Plan& out) {
     if (c->max_dyn == 0) {
         size_t st = 0;
         cudaError_t e = qs_kernel_static_smem(&st);
@@ -153,23 +153,23 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, Plan& out) {
         if (e != cudaSuccess) return cuda_fail(c, e, "cudaFuncSetAttribute");
         c->attrs_smem = c->max_dyn;
     }
-    const int sizes[6] = {1, 2, 4, 6, 8, 16};
+    const int sizes[7] = {1, 2, 4, 5, 6, 8, 16};
     int first = -1;
-    for (int i = 0; i < 6; ++i) {
+    for (int i = 0; i < 7; ++i) {
         const int n_s = qs::align_up((V + sizes[i] - 1) / sizes[i], 8);
-        if ((size_t)qs::smem_layout(n_s).total <= c->max_dyn) {
+        if ((size_t)qs::smem_layout(n_s, vcounts).total <= c->max_dyn) {
             first = i;
             break;
         }
     }
     if (first < 0)
         return fail(c, QSAMP_ERR_UNSUPPORTED, "V=%d exceeds the largest vocabulary one 16-CTA cluster holds (%d)", V,
-                    16 * (int)((c->max_dyn - (size_t)qs::smem_layout(0).total) / 4 / 8 * 8));
+                    16 * (int)((c->max_dyn - (size_t)qs::smem_layout(0, vcounts).total) / 4 / 8 * 8));
     int pick = first;
-    for (int i = first; i < 6; ++i) {
+    for (int i = first; i < 7; ++i) {
         const int cl = sizes[i];
         const int n_s = qs::align_up((V + cl - 1) / cl, 8);
-        const size_t smem = (size_t)qs::smem_layout(n_s).total;
+        const size_t smem = (size_t)qs::smem_layout(n_s, vcounts).total;
         int mc = 0;
         cudaError_t e = qs_max_clusters(cl, smem, &mc);
         if (e != cudaSuccess) {
@@ -183,7 +183,7 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, Plan& out) {
     const int cl = sizes[pick];
     out.cl = cl;
     out.n_s = qs::align_up((V + cl - 1) / cl, 8);
-    out.smem = (size_t)qs::smem_layout(out.n_s).total;
+    out.smem = (size_t)qs::smem_layout(out.n_s, vcounts).total;
     int mc = 0;
     cudaError_t e = qs_max_clusters(cl, out.smem, &mc);
     if (e != cudaSuccess || mc <= 0)
@@ -504,14 +504,15 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     }
     if (n_cluster > 0) {
         Plan plan;
-        s = plan_for(c, n_cluster, b->V, plan);
+        s = plan_for(c, n_cluster, b->V, b->dtype == QSAMP_BF16, plan);
         if (s != QSAMP_OK) return s;
         if (n_stream > 0) {
             // the SMs split by the rows' expected work (measured on B200, V=151936):
             // a stream row takes about 48 SM-us (half an SM for ~95 us), a
-            // cluster row about 140 us on each of its CTAs' SMs; clusters leave
-            // the stream kernel its share
-            const double ws = 48.0 * n_stream, wc = 140.0 * plan.cl * n_cluster;
+            // cluster row about 140 us on each of its 6 CTAs' SMs, of which
+            // 0.45 scales with the slice (1 / cl) and 0.55 does not; clusters
+            // leave the stream kernel its share
+            const double ws = 48.0 * n_stream, wc = 140.0 * (0.55 * plan.cl + 2.7) * n_cluster;
             const int reserve = (int)std::ceil(c->num_sms * ws / (ws + wc));
             const int cap = (c->num_sms - reserve) / plan.cl;
             plan.clusters = std::max(1, std::min(plan.clusters, cap));

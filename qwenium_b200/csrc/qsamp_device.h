@@ -111,7 +111,9 @@ struct __align__(16) Misc {
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-__host__ __device__ inline SmemLayout smem_layout(int n_s) {
+// vcounts: the per-bin counts of the smallest / largest value (bf16 rows,
+// whose equal logits fill whole bins); fp32 layouts leave them out.
+__host__ __device__ inline SmemLayout smem_layout(int n_s, bool vcounts = true) {
     SmemLayout L;
     int o = 0;
     L.off_vals = o;   o = align_up(o + n_s * 4, 16);
@@ -126,7 +128,7 @@ __host__ __device__ inline SmemLayout smem_layout(int n_s) {
     L.off_tie = o;    o = align_up(o + NB / 8, 16);
     L.off_vmin = o;   o = align_up(o + NB * 4, 16);     // smallest / largest value key per bin:
     L.off_vmax = o;   o = align_up(o + NB * 4, 16);     // equal = every element of the bin has one value
-    L.off_vcnt = o;   o = align_up(o + NB * 4, 16);     // counts at vmax (low 16 bits) / vmin (high 16 bits)
+    L.off_vcnt = o;   o = align_up(o + (vcounts ? NB * 4 : 0), 16);  // counts at vmax (low 16 bits) / vmin (high 16 bits)
     L.off_spec = o;   o = align_up(o + SPEC_CAP * 8, 16);
     L.off_spect = o;  o = align_up(o + SPEC_CAP * 4, 16);
     L.off_exp = o;    o = align_up(o + 32 * 8, 16);        // expf's 2^(i/32) table

@@ -110,7 +110,7 @@ __device__ __forceinline__ bool uniform_bin(const uint32_t* cnt, const uint32_t*
 // A bin whose elements hold exactly two values: two runs of equal terms.
 __device__ __forceinline__ bool twoval_bin(const uint32_t* cnt, const uint32_t* vmin, const uint32_t* vmax,
                                            const uint32_t* vcnt, int b) {
-    if (b >= NB - 1 || cnt[b] == 0 || vmin[b] == vmax[b]) return false;
+    if (!vcnt || b >= NB - 1 || cnt[b] == 0 || vmin[b] == vmax[b]) return false;
     const uint32_t a = vcnt[b] & 0xffffu, c = vcnt[b] >> 16;
     return a < 0xffffu && c < 0xffffu && a + c == cnt[b];
 }
@@ -142,8 +142,8 @@ __device__ __forceinline__ BinRuns bin_runs(const uint32_t* cnt, const uint32_t*
 }
 #define BIN_RUNS(b) bin_runs(s.cnt, s.vmin, s.vmax, s.vcnt, (b), M)
 
-__device__ __forceinline__ Sm carve(unsigned char* base, int n_s) {
-    const SmemLayout L = smem_layout(n_s);
+__device__ __forceinline__ Sm carve(unsigned char* base, int n_s, bool vcounts) {
+    const SmemLayout L = smem_layout(n_s, vcounts);
     Sm s;
     s.vals = (float*)(base + L.off_vals);
     s.cnt = (uint32_t*)(base + L.off_cnt);
@@ -163,7 +163,7 @@ __device__ __forceinline__ Sm carve(unsigned char* base, int n_s) {
     s.tie = (uint32_t*)(base + L.off_tie);
     s.vmin = (uint32_t*)(base + L.off_vmin);
     s.vmax = (uint32_t*)(base + L.off_vmax);
-    s.vcnt = (uint32_t*)(base + L.off_vcnt);
+    s.vcnt = vcounts ? (uint32_t*)(base + L.off_vcnt) : nullptr;
     s.spec = (unsigned long long*)(base + L.off_spec);
     s.spect = (float*)(base + L.off_spect);
     s.exp32 = (const uint64_t*)(base + L.off_exp);
@@ -1556,7 +1556,7 @@ __device__ void cluster_reduce_bins(cg::cluster_group& cl, const Sm& s, bool cnt
             st4(s.cnt, b, c[0], c[1], c[2], c[3]);
             st4(s.vmin, b, lo[0], lo[1], lo[2], lo[3]);
             st4(s.vmax, b, hi[0], hi[1], hi[2], hi[3]);
-            st4(s.vcnt, b, vc[0], vc[1], vc[2], vc[3]);
+            if (vcounts) st4(s.vcnt, b, vc[0], vc[1], vc[2], vc[3]);
             st4((uint32_t*)s.tsum, b, tf[0], tf[1], tf[2], tf[3]);
         }
     }
@@ -1702,25 +1702,24 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, doub
 
 // The exact part of a pass for one element of bin b (b < NB - 1): t =
 // expf(x), its t sum (first pass) and its integer k-sum term (needk).
+__device__ __forceinline__ void pass_ksum(const Sm& s, float t, int b, int kmode, float Sn) {
+    // k-sums as two u32 limbs (k mod 2^16, k / 2^16): no carries, so the
+    // adds need no returned value; a half-way or >= 2^24 term makes the
+    // bin unwalkable
+    int tie, big;
+    const uint32_t kk = kmode == 1 ? qs_kround(t, s.gs[b], &tie, &big) : qs_kround(__fdiv_rn(t, Sn), s.gc[b], &tie, &big);
+    if (tie | big) {
+        atomicOr(&s.tie[b >> 5], 1u << (b & 31));
+    } else {
+        atomicAdd(&s.ksum_lo[b], kk & 0xffffu);
+        if (kk >> 16) atomicAdd(&s.ksum_hi[b], kk >> 16);
+    }
+}
 __device__ __forceinline__ void pass_heavy(const Sm& s, float x, int b, bool first, bool needk, int kmode, float Sn) {
     const float t = qs_expf_tab(x, s.exp32);
     if (first) smem_add_u64(&s.tx_lo[b], &s.tx_hi[b], qs_fixed40(t));
-    if (needk) {
-        // k-sums as two u32 limbs (k mod 2^16, k / 2^16): no carries, so the
-        // adds need no returned value; a half-way or >= 2^24 term makes the
-        // bin unwalkable
-        int tie, big;
-        const uint32_t kk = kmode == 1 ? qs_kround(t, s.gs[b], &tie, &big)
-                                       : qs_kround(__fdiv_rn(t, Sn), s.gc[b], &tie, &big);
-        if (tie | big) {
-            atomicOr(&s.tie[b >> 5], 1u << (b & 31));
-        } else {
-            atomicAdd(&s.ksum_lo[b], kk & 0xffffu);
-            if (kk >> 16) atomicAdd(&s.ksum_hi[b], kk >> 16);
-        }
-    }
+    if (needk) pass_ksum(s, t, b, kmode, Sn);
 }
-
 // One pass of a CTA over its slice: the bin of every finite element; the
 // exact t sums (first pass) and integer k-sums of the bins [kfrom, kto] whose
 // flag has the pass's plain bit (kmode 1: S walk at binade gs, kmode 2:
@@ -1824,10 +1823,11 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
         s.tsum32[b] = 0u;
         s.vmin[b] = 0xffffffffu;
         s.vmax[b] = 0u;
-        s.vcnt[b] = 0u;
+        if (s.vcnt) s.vcnt[b] = 0u;
     }
     __syncthreads();
     int ninf = 0, ntail = 0;
+#pragma unroll 4
     for (int i = threadIdx.x; i < r.len; i += NT) {
         const float v = s.vals[i];
         if (v == NEG_INF) { ++ninf; continue; }
@@ -2426,7 +2426,7 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
     const int cid = blockIdx.x / CL;
     const int ncl = gridDim.x / CL;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const Sm s = carve(smem_raw, a.n_s);
+    const Sm s = carve(smem_raw, a.n_s, a.dtype == QSAMP_BF16);
     if (threadIdx.x < 32) ((uint64_t*)s.exp32)[threadIdx.x] = qs_tab_exp32_d[threadIdx.x];
     Misc* m = s.misc;
     const float NEG_INF = -__int_as_float(0x7f800000);
