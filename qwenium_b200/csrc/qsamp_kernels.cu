@@ -33,7 +33,7 @@ namespace cg = cooperative_groups;
 // row's leading CTA records %globaltimer into qs_phase[row][slot]. Expands to
 // nothing in the shipped library.
 #ifdef QS_PHASE_TIMING
-__device__ unsigned long long qs_phase[8192][40];
+__device__ unsigned long long qs_phase[8192][48];
 #define QS_TMARK(row, slot, lead)                                                 \
     do {                                                                         \
         if (threadIdx.x == 0 && (lead) && (row) < 8192) {                        \
@@ -42,9 +42,17 @@ __device__ unsigned long long qs_phase[8192][40];
             qs_phase[(row)][(slot)] = t_;                                        \
         }                                                                        \
     } while (0)
+// QS_NOTE stores a value (a list length) instead of a time.
+#define QS_NOTE(row, slot, val, lead)                                           \
+    do {                                                                         \
+        if (threadIdx.x == 0 && (lead) && (row) < 8192) qs_phase[(row)][(slot)] = (unsigned long long)(val); \
+    } while (0)
 #else
 #define QS_TMARK(row, slot, lead) \
     do {                          \
+    } while (0)
+#define QS_NOTE(row, slot, val, lead) \
+    do {                              \
     } while (0)
 #endif
 // Sub-phase cycle counts (profiling builds): QS_SUB(row, j, lead) adds the
@@ -1644,12 +1652,13 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, doub
     // result (the walk verifies every bin); a wide window in a sparse tail
     // would gather thousands of elements.
     const double D = 2e-3, Dc = 2e-4, Dd = 5e-4, pp = top_p;
+    const double sc = ratio / Sn;  // (predictions: a product in place of a quotient per bin)
     __shared__ int pc_bcut;
     if (threadIdx.x == 0) pc_bcut = NB - 1;
     __syncthreads();
     for (int b = threadIdx.x; b < NB - 1; b += NT) {
         if (s.cnt[b] == 0) continue;
-        const double ca = s.pref[b] / Sn * ratio, cb = (s.pref[b] + (double)TX(b) * 0x1p-40) / Sn * ratio;
+        const double ca = s.pref[b] * sc, cb = (s.pref[b] + (double)TX(b) * 0x1p-40) * sc;
         if (cb >= pp - Dc && ca <= pp + Dc) atomicMin(&pc_bcut, b);
     }
     __syncthreads();
@@ -1661,7 +1670,7 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, doub
     for (int b = threadIdx.x; b < NB; b += NT) {
         uint8_t f = (uint8_t)(s.flag[b] & ~(F_PLAINC | F_WANT));
         if (b < NB - 1 && s.cnt[b] > 0) {
-            const double ca = s.pref[b] / Sn * ratio, cb = (s.pref[b] + (double)TX(b) * 0x1p-40) / Sn * ratio;
+            const double ca = s.pref[b] * sc, cb = (s.pref[b] + (double)TX(b) * 0x1p-40) * sc;
             const bool draw = cb >= dlo && ca <= dhi && (int)s.cnt[b] <= SPEC_CAP / 2;
             if (b >= from) {
                 if (ca <= pp + 1e-2) {
@@ -1877,6 +1886,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
         const double u = row_u(a, r.row, p);
         const double pp = pa ? (double)p.top_p : 1.0;
         const double D = 2e-3;
+        const double inv_est = 1.0 / S_est;
         const long long topn = (a.top_ids && a.top_cap > 0) ? a.top_cap : 0;
         for (int b = threadIdx.x; b < NB; b += NT) {
             uint8_t f = 0;
@@ -1892,7 +1902,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     g = (int8_t)binade_d(Pa);
                     cross = binade_d(Pa * (1 - D)) != binade_d(Pb * (1 + D));
                 }
-                const double ca = Pa / S_est, cb = Pb / S_est;
+                const double ca = Pa * inv_est, cb = Pb * inv_est;
                 if (RUNBIN(b)) want = cross = false;
                 // ... and ids: the predicted draw (rows without top-p: the
                 // cumulative pass of a top-p row gathers its own) and the top list
@@ -1991,13 +2001,17 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
             QS_SUB(r.row, 0, true);
             {
                 const int n = m->spec_n < SPEC_CAP ? m->spec_n : SPEC_CAP;
+                if (it_no < 5) QS_NOTE(r.row, 35 + it_no, m->spec_n, true);
                 const int P2 = next_pow2(n > 1 ? n : 1);
                 for (int i = n + threadIdx.x; i < P2; i += NT) s.spec[i] = 0ull;
                 __syncthreads();
-                bitonic_desc<256>(s.spec, P2);
+                QS_SUB(r.row, 16, true);
+                if (P2 > 1) bitonic_desc<256>(s.spec, P2);
+                QS_SUB(r.row, 17, true);
                 for (int i = threadIdx.x; i < n; i += NT) s.spect[i] = qs_expf_tab(__fsub_rn(comp_val(s.spec[i]), M), s.exp32);
             }
             __syncthreads();
+            QS_SUB(r.row, 18, true);
             if (threadIdx.x == 0) {
                 m->first_round = 0;
                 m->kmode = 0;
@@ -2258,11 +2272,12 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     // the cutoff bin by its survivors (mass_cut).
                     const int bc = w.cut_all ? NB : w.cut_bin;
                     const double Sc = (double)w.Sc;
+                    const double isc = 1.0 / Sc;  // bin masses (the draw bin's search; its elements use t / Sc)
                     const long long c = w.n_keep;
                     double* mpre = s.pref;
                     double dsum = 0.0;
                     block_bin_prefix<double>([&](int b) {
-                        return b < bc ? (double)TX(b) * 0x1p-40 / Sc : (b == bc ? w.mass_cut : 0.0);
+                        return b < bc ? (double)TX(b) * 0x1p-40 * isc : (b == bc ? w.mass_cut : 0.0);
                     }, mpre, m, &dsum);
                     uint32_t* cpre = (uint32_t*)s.sstart;  // the S walk's starts are no longer needed
                     block_bin_prefix<uint32_t>([&](int b) { return s.cnt[b]; }, cpre, m, (uint32_t*)nullptr);
@@ -2273,7 +2288,7 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     __syncthreads();
                     const double tgt = d_tgt;
                     for (int b = threadIdx.x; b < NB && b <= bc; b += NT) {
-                        const double mb = b < bc ? (double)TX(b) * 0x1p-40 / Sc : w.mass_cut;
+                        const double mb = b < bc ? (double)TX(b) * 0x1p-40 * isc : w.mass_cut;
                         if (s.cnt[b] > 0 && (c < 2 || mpre[b] + mb >= tgt)) atomicMin(&d_bin, b);
                     }
                     __syncthreads();
@@ -2498,17 +2513,26 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
         if (threadIdx.x == 0) { m->cmax = bm; m->cmax_idx = bidx; }
         __syncthreads();
         cl.sync();
-        if (threadIdx.x == 0) {
+        if (threadIdx.x < 32) {
+            // lane q reads CTA q's maximum (the peers' loads overlap); the
+            // largest value, lowest id among equals
             float gm = NEG_INF;
             int gi = 0x7fffffff;
-            for (int q = 0; q < CL; ++q) {
+            for (int q = threadIdx.x; q < CL; q += 32) {
                 const Misc* pm = peer(cl, m, q);
                 const float v = pm->cmax;
                 const int i = pm->cmax_idx;
                 if (v > gm || (v == gm && i < gi)) { gm = v; gi = i; }
             }
-            m->M = gm;
-            m->argmax = gi == 0x7fffffff ? 0 : gi;
+            for (int o = 16; o > 0; o >>= 1) {
+                const float v = __shfl_down_sync(FULLMASK, gm, o);
+                const int i = __shfl_down_sync(FULLMASK, gi, o);
+                if (v > gm || (v == gm && i < gi)) { gm = v; gi = i; }
+            }
+            if (threadIdx.x == 0) {
+                m->M = gm;
+                m->argmax = gi == 0x7fffffff ? 0 : gi;
+            }
         }
         __syncthreads();
 
@@ -3514,7 +3538,7 @@ extern "C" cudaError_t qs_launch_stream(const qs::QsLaunch* a, int grid, size_t 
 #ifdef QS_PHASE_TIMING
 extern "C" cudaError_t qs_phase_read(void* host) { return cudaMemcpyFromSymbol(host, qs_phase, sizeof(qs_phase)); }
 extern "C" cudaError_t qs_phase_clear() {
-    static unsigned long long z[8192][40];
+    static unsigned long long z[8192][48];
     return cudaMemcpyToSymbol(qs_phase, z, sizeof(z));
 }
 #endif
