@@ -42,6 +42,19 @@ __device__ unsigned long long qs_phase[8192][48];
             qs_phase[(row)][(slot)] = t_;                                        \
         }                                                                        \
     } while (0)
+// QS_RACC_*: clock64 sums kept in registers of one thread (loops), stored once.
+#define QS_RACC_DECL(n) long long qs_racc[n] = {}; long long qs_rt = clock64()
+#define QS_RACC(j)                          \
+    do {                                    \
+        const long long t_ = clock64();     \
+        qs_racc[(j)] += t_ - qs_rt;         \
+        qs_rt = t_;                         \
+    } while (0)
+#define QS_RACC_STORE(row, slot, n, lead)                                                      \
+    do {                                                                                       \
+        if (threadIdx.x == 0 && (lead) && (row) < 8192)                                        \
+            for (int j_ = 0; j_ < (n); ++j_) qs_phase[(row)][(slot) + j_] = (unsigned long long)qs_racc[j_]; \
+    } while (0)
 // QS_NOTE stores a value (a list length) instead of a time.
 #define QS_NOTE(row, slot, val, lead)                                           \
     do {                                                                         \
@@ -53,6 +66,15 @@ __device__ unsigned long long qs_phase[8192][48];
     } while (0)
 #define QS_NOTE(row, slot, val, lead) \
     do {                              \
+    } while (0)
+#define QS_RACC_DECL(n) \
+    do {                \
+    } while (0)
+#define QS_RACC(j) \
+    do {           \
+    } while (0)
+#define QS_RACC_STORE(row, slot, n, lead) \
+    do {                                  \
     } while (0)
 #endif
 // Sub-phase cycle counts (profiling builds): QS_SUB(row, j, lead) adds the
@@ -1709,6 +1731,22 @@ __device__ void predict_c(const Sm& s, int from, double ratio, float top_p, doub
     __syncthreads();
 }
 
+// qs_kround and qs_fixed40 in float arithmetic: for 0 <= p <= 1 the product
+// p * 2^n (23 - g or 40) is exact in float (a power-of-two scaling that
+// neither overflows nor drops bits), so rintf (round half to even) and a
+// truncating conversion give the integer forms' results (tests/math_check.c
+// checks the integer forms against exactly these float definitions over
+// every float in [0, 1]). A binade outside the exact range takes the
+// integer form.
+__device__ __forceinline__ uint32_t kround_f(float p, int g, int* tie, int* big) {
+    if (g < -100 || g > 140) return qs_kround(p, g, tie, big);
+    const float y = __fmul_rn(p, pow2f(23 - g));
+    *big = !(y < 16777216.0f);
+    *tie = (y - floorf(y)) == 0.5f;
+    return *big ? 0u : (uint32_t)rintf(y);
+}
+__device__ __forceinline__ unsigned long long fixed40_f(float t) { return __float2ull_rz(__fmul_rn(t, 0x1p40f)); }
+
 // The exact part of a pass for one element of bin b (b < NB - 1): t =
 // expf(x), its t sum (first pass) and its integer k-sum term (needk).
 __device__ __forceinline__ void pass_ksum(const Sm& s, float t, int b, int kmode, float Sn) {
@@ -1716,7 +1754,7 @@ __device__ __forceinline__ void pass_ksum(const Sm& s, float t, int b, int kmode
     // adds need no returned value; a half-way or >= 2^24 term makes the
     // bin unwalkable
     int tie, big;
-    const uint32_t kk = kmode == 1 ? qs_kround(t, s.gs[b], &tie, &big) : qs_kround(__fdiv_rn(t, Sn), s.gc[b], &tie, &big);
+    const uint32_t kk = kmode == 1 ? kround_f(t, s.gs[b], &tie, &big) : kround_f(__fdiv_rn(t, Sn), s.gc[b], &tie, &big);
     if (tie | big) {
         atomicOr(&s.tie[b >> 5], 1u << (b & 31));
     } else {
@@ -1726,7 +1764,7 @@ __device__ __forceinline__ void pass_ksum(const Sm& s, float t, int b, int kmode
 }
 __device__ __forceinline__ void pass_heavy(const Sm& s, float x, int b, bool first, bool needk, int kmode, float Sn) {
     const float t = qs_expf_tab(x, s.exp32);
-    if (first) smem_add_u64(&s.tx_lo[b], &s.tx_hi[b], qs_fixed40(t));
+    if (first) smem_add_u64(&s.tx_lo[b], &s.tx_hi[b], fixed40_f(t));
     if (needk) pass_ksum(s, t, b, kmode, Sn);
 }
 // One pass of a CTA over its slice: the bin of every finite element; the
@@ -2665,6 +2703,7 @@ constexpr int SN_SLACK = 256;              // compaction once k + SN_SLACK are h
 constexpr int SN_HMAX = 1024;              // penalty window this kernel takes
 constexpr int SN_HT = 2 * SN_HMAX;         // window hash table slots (power of two)
 constexpr int SN_G = 4;                    // chunks per super-chunk (one barrier each)
+constexpr int SN_PF = 4;                   // chunks prefetched into L2 ahead of the loads
 static_assert(SN_PER == 8 && SN_G * SN_PER <= 32 && SN_CAP % SN_NT == 0, "stream kernel shape");
 // appends past SN_CAP - SN_HMAX wait for a compaction, which the trigger
 // (at most SN_CAP - SN_HMAX - 512 held) requests first
@@ -2860,6 +2899,19 @@ __device__ __forceinline__ bool sn_append(unsigned long long* cand, int* n, int 
 }
 
 // The SN_PER consecutive elements from i0 (raw logits and bf16 bits).
+// Thread 0: chunk c of the row into L2 (cp.async.bulk.prefetch; no registers
+// or shared memory), its bytes rounded down to 16 within the row. Rows are
+// 16-byte aligned (vec).
+__device__ __forceinline__ void sn_prefetch(const RowCtx& r, int c, int V) {
+    const int i0 = c * SN_CH;
+    if (i0 >= V) return;
+    const int n = V - i0 < SN_CH ? V - i0 : SN_CH;
+    const uint32_t esz = r.dtype == QSAMP_BF16 ? 2u : 4u;
+    const uint32_t bytes = ((uint32_t)n * esz) & ~15u;
+    if (bytes == 0u) return;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((const char*)r.rowp + (size_t)i0 * esz), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void sn_load(const RowCtx& r, bool vec, int i0, int V, float (&x)[SN_PER],
                                         uint32_t (&b)[SN_PER]) {
     if (vec && i0 + SN_PER <= V) {
@@ -3021,13 +3073,17 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
         const int j0 = SN_PER * threadIdx.x;
         float xn[SN_PER];
         uint32_t bn[SN_PER];
+        if (vec && threadIdx.x == 0)
+            for (int c = 1; c <= SN_PF && c < nchunks; ++c) sn_prefetch(r, c, V);
         sn_load(r, vec, j0, V, xn, bn);
+        QS_RACC_DECL(4);
         for (int c = 0; c < nchunks; ++c) {
             const int i0 = c * SN_CH + j0;
             float x[SN_PER];
             uint32_t b16[SN_PER];
 #pragma unroll
             for (int e = 0; e < SN_PER; ++e) { x[e] = xn[e]; b16[e] = bn[e]; }
+            if (vec && threadIdx.x == 0 && c + 1 + SN_PF < nchunks) sn_prefetch(r, c + 1 + SN_PF, V);
             if (c + 1 < nchunks) sn_load(r, vec, i0 + SN_CH, V, xn, bn);
             if (greedy) {
                 if (i0 < V) {
@@ -3050,6 +3106,7 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
                 for (int e = 0; e < SN_PER; ++e)
                     if (i0 + e < V && !(x[e] < xt)) lm |= 1u << e;
                 const int g = c - sc_first;  // sub-chunk of the current super-chunk
+                QS_RACC(0);
                 if (__any_sync(FULLMASK, lm != 0u)) {
                     if (nuniq && lm) lm &= ~(bitmap[i0 >> 5] >> (i0 & 31));  // window ids: folded in later
                     const unsigned long long tau = sh_tau;
@@ -3072,6 +3129,7 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
                         if (sn_append(cand, &sh_n, cap, trig, ok, cc, over)) pend |= 1u << (g * SN_PER + e);
                     }
                 }
+                QS_RACC(1);
                 // a super-chunk ends with the row's first chunk, every SN_G
                 // chunks and with the row: the list is compacted there when
                 // an appender crossed the trigger (the barrier's own OR, the
@@ -3106,6 +3164,7 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
                     }
                     sc_first = c + 1;
                 }
+                QS_RACC(2);
             }
         }
 
@@ -3134,6 +3193,7 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
             }
         }
         QS_TMARK(row, 2, true);
+        QS_RACC_STORE(row, 24, 3, true);
         // clear the window's bitmap words for the next row (the tail below
         // reuses the hash table as scratch)
         __syncthreads();

@@ -115,6 +115,28 @@ def run(seed: int = 1000, B_rows: int = 256, sm_mhz: float = 1965.0) -> None:
     end = max(d["start"] + d["total"] for d in rows)
     print(f"work {sum(d['total'] for d in rows):.0f} us over the rows, span {end:.1f} us")
 
+    # stream kernel rows (one CTA per row): marks 0-4 only
+    srow = [r for r in range(B_rows) if ph[r, 0] != 0 and ph[r, 5] == 0 and ph[r, 4] != 0]
+    if srow:
+        p = cfg["params"]
+        st_rows = [dict(k=int(p["top_k"][r]), win=us(ph[r, 1] - ph[r, 0]), stream=us(ph[r, 2] - ph[r, 1]),
+                        select=us(ph[r, 3] - ph[r, 2]), finish=us(ph[r, 4] - ph[r, 3]), total=us(ph[r, 4] - ph[r, 0]),
+                        start=us(ph[r, 0] - t0)) for r in srow]
+        print(f"rows on the stream kernel: {len(st_rows)}")
+        # thread 0's clock64 sums over the chunk loop: loads + raw filter, exact path, super-chunk barriers
+        for j, name in enumerate(["loads + raw filter", "exact path", "barriers + compactions"]):
+            v = statistics.mean(ph[r, 24 + j] for r in srow) / sm_mhz
+            print(f"  stream loop: {name:21s} {v:7.1f} us")
+        for k, name in [("win", "penalty window table"), ("stream", "stream of the row"),
+                        ("select", "last compaction + sort"), ("finish", "top-p, softmax, draw"),
+                        ("total", "whole row")]:
+            print(f"  {name:28s} {statistics.mean(d[k] for d in st_rows):7.1f} us")
+        for kk in sorted({d["k"] for d in st_rows}):
+            sel = [d for d in st_rows if d["k"] == kk]
+            print(f"  top_k {kk:4d}: {len(sel):3d} rows, stream {statistics.mean(d['stream'] for d in sel):6.1f} us, "
+                  f"whole row {statistics.mean(d['total'] for d in sel):6.1f} us")
+        print(f"  span {max(d['start'] + d['total'] for d in st_rows):.1f} us")
+
 
 if __name__ == "__main__":
     if "--build" in sys.argv:
