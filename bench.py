@@ -38,6 +38,7 @@ sys.path.insert(0, ROOT)
 B_DEFAULT = 256
 V = 151936
 HIST = 256
+BATCH_SEED = 1000  # the config2-B256 batch every rank serves
 
 
 def env_int(k, d):
@@ -157,7 +158,11 @@ def run_gpu(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     B = args.batch
-    cfg = W.config2(seed=1000 + rank, B=B)
+    # weak scaling: every rank serves the same seeded batch of B rows on its
+    # own GPU (fixed work per GPU; batches of other seeds differ in their mix
+    # of full-vocabulary rows, and the max over ranks would then time the
+    # heaviest batch rather than the scaling)
+    cfg = W.config2(seed=BATCH_SEED, B=B)
     ctx = qsamp.Context(local)
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream(dev)
@@ -288,6 +293,7 @@ def run_gpu(args):
         "data": "synthetic (seeded config-2 distribution)",
         "config": {"workload": "config2-B256: batched server decode parameters at B=256, V=151936 fp32",
                    "B_per_gpu": B, "V": V, "history": HIST, "parallelism": f"rows x{world}",
+                   "batch_seed": BATCH_SEED,
                    "l2": f"rotating {ncopies} input copies ({ncopies * bytes_one / 1e6:.0f} MB) > L2"},
         "e2e": {"value": round(e2e_rows_s, 1) if e2e_rows_s else None, "unit": "rows/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
