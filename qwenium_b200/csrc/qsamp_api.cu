@@ -153,9 +153,10 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, bool vcounts, Plan& out) {
         if (e != cudaSuccess) return cuda_fail(c, e, "cudaFuncSetAttribute");
         c->attrs_smem = c->max_dyn;
     }
-    const int sizes[7] = {1, 2, 4, 5, 6, 8, 16};
+    // (a GPC holds two clusters of 9 or 10 CTAs but only one of 12 or 16)
+    const int sizes[10] = {1, 2, 4, 5, 6, 8, 9, 10, 12, 16};
     int first = -1;
-    for (int i = 0; i < 7; ++i) {
+    for (int i = 0; i < 10; ++i) {
         const int n_s = qs::align_up((V + sizes[i] - 1) / sizes[i], 8);
         if ((size_t)qs::smem_layout(n_s, vcounts).total <= c->max_dyn) {
             first = i;
@@ -166,7 +167,7 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, bool vcounts, Plan& out) {
         return fail(c, QSAMP_ERR_UNSUPPORTED, "V=%d exceeds the largest vocabulary one 16-CTA cluster holds (%d)", V,
                     16 * (int)((c->max_dyn - (size_t)qs::smem_layout(0, vcounts).total) / 4 / 8 * 8));
     int pick = first;
-    for (int i = first; i < 7; ++i) {
+    for (int i = first; i < 10; ++i) {
         const int cl = sizes[i];
         const int n_s = qs::align_up((V + cl - 1) / cl, 8);
         const size_t smem = (size_t)qs::smem_layout(n_s, vcounts).total;
