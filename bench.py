@@ -350,6 +350,16 @@ def run_extras(ctx, dev, stream):
         f4(i)
     ms = _events_ms(stream, f4, 5)
     out["config4_B256"] = {"ms_per_call": round(ms, 4), "rows_per_s": round(256 / (ms * 1e-3), 1)}
+    # C4 at B=1024 (its own seeded batch; two copies on the device, 1.07 GB)
+    del xs
+    c4 = W.config4(4, B=1024)
+    xs = [torch.from_numpy(np.ascontiguousarray(c4["logits"]).view(np.int16)).to(dev) for _ in range(2)]
+    h4 = torch.from_numpy(c4["hist"]).to(dev)
+    for i in range(2):
+        f4(i)
+    ms = _events_ms(stream, f4, 3)
+    out["config4_B1024"] = {"ms_per_call": round(ms, 4), "rows_per_s": round(1024 / (ms * 1e-3), 1)}
+    del xs, h4
     # greedy verification: 128 slots x 5 drafts, V=151936 fp32
     rng = np.random.default_rng(0)
     n, K = 640, 5
