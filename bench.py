@@ -136,7 +136,7 @@ def stream_rows(params, V_, window=HIST):
 
 
 def algorithmic_bytes_per_row(V_, hist_len, bytes_per_logit=4, mask=False):
-    # logits + history ids + params/u/result (SURVEY 8d per-row figure)
+    # logits + allow-mask words + history ids + params/u/result per row
     return V_ * bytes_per_logit + (((V_ + 31) // 32) * 4 if mask else 0) + 4 * hist_len + 64
 
 

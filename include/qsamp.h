@@ -110,11 +110,45 @@ qsamp_status qsamp_sample(qsamp_ctx* ctx, const qsamp_batch* batch, void* stream
  * logits live on the host. */
 qsamp_status qsamp_sample_host(qsamp_ctx* ctx, const qsamp_batch* batch);
 
+/* Device-side outcome of the most recent qsamp_sample, qsamp_shard_topk or
+ * qsamp_merge_topk call on this context. Those calls are asynchronous and
+ * return before the kernels run; each ends with a stream-ordered copy of the
+ * kernels' status word into pinned host memory, which this function reads.
+ * Call it after synchronising that call's stream. QSAMP_OK, or
+ * QSAMP_ERR_DEVICE with qsamp_last_error naming the limit that was hit (a
+ * gather-round budget, a bounded wait that ran out); the rows concerned
+ * carry token -1. The reference throws where a row cannot be sampled
+ * (sampling.cpp:101,140): a caller that replaces Sampler::sample with
+ * qsamp_sample converts QSAMP_ERR_DEVICE into that throw.
+ * (qsamp_sample_host reads the status itself and returns it.) */
+qsamp_status qsamp_poll_status(qsamp_ctx* ctx);
+
+/* Device-side limits of a context (no counterpart in the reference). The
+ * kernels never wait without a bound; these set the bounds:
+ *   max_rounds      gather rounds a full-vocabulary row may take before it
+ *                   is given up (token -1, QSAMP_ERR_DEVICE); default 64,
+ *                   at least 1.
+ *   ready_wait_ns   qsamp_sample_host copies the logits in row chunks while
+ *                   the kernels run; a kernel waits at most this long for a
+ *                   chunk's arrival flag before it gives the row up
+ *                   (token -1); default 1e9 (one second), at least 1000.
+ *   drop_ready_from fault injection for tests: chunks with index >= this
+ *                   value never raise their arrival flag (their bytes are
+ *                   still copied), so the kernels' bounded waits run out;
+ *                   -1 (the default) turns it off. */
+typedef struct qsamp_limits {
+    int32_t max_rounds;
+    int32_t drop_ready_from;
+    int64_t ready_wait_ns;
+} qsamp_limits;
+qsamp_status qsamp_set_limits(qsamp_ctx* ctx, const qsamp_limits* limits);
+qsamp_status qsamp_get_limits(const qsamp_ctx* ctx, qsamp_limits* out);
+
 /* Allocation-free selection. No counterpart in the reference: it exists
  * for callers that may not allocate device memory when they sample (a
- * serving engine that reserves all device memory up front, a plugin host
- * that forbids cudaMalloc, code running under someone else's graph-capture
- * rules). qsamp_create allocates, so this entry point takes no context.
+ * serving engine that reserves all device memory up front for its own
+ * allocator, a plugin host that forbids cudaMalloc). qsamp_create
+ * allocates, so this entry point takes no context.
  *
  * Same batch semantics as qsamp_sample (logits, hist, masks and outputs in
  * device memory; params, hist_len and u on the host). Its scratch is one
@@ -125,7 +159,9 @@ qsamp_status qsamp_sample_host(qsamp_ctx* ctx, const qsamp_batch* batch);
  * logit). The first call on a device, with that device current, looks up the
  * array's device address; make it before any stream capture. All calls on a
  * device share the array, so calls whose work overlaps on the GPU race.
- * Device-side limits are reported in the row results (token -1). err, when
+ * Device-side limits (the gather-round budget of a full-vocabulary row, a
+ * slice copy that did not complete) are reported only in the row results:
+ * token -1 for that row; the call has no other channel for them. err, when
  * non-NULL, receives a message of at most err_len bytes. */
 #define QSAMP_STATIC_MAX_ROWS 4096
 #define QSAMP_STATIC_SCRATCH_BYTES (640u * 1024u)
@@ -242,6 +278,12 @@ typedef struct qsamp_counters {
     double last_stream_kernel_ms; /* greedy / top-k rows, and vocab shards */
     double last_rows_kernel_ms;   /* full-vocabulary rows (cluster kernel) */
     double last_merge_kernel_ms;  /* qsamp_merge_topk */
+    /* routing and launch shape of the last qsamp_sample / qsamp_sample_host
+     * call: rows served by the stream kernel and by the cluster kernel, the
+     * cluster kernel's CTAs per cluster and clusters launched (0 when it did
+     * not run) */
+    int32_t last_stream_rows, last_cluster_rows;
+    int32_t last_cluster_size, last_clusters;
 } qsamp_counters;
 qsamp_status qsamp_get_counters(const qsamp_ctx* ctx, qsamp_counters* out);
 qsamp_status qsamp_set_kernel_timing(qsamp_ctx* ctx, int32_t on);

@@ -283,3 +283,54 @@ class RefGrammar:
             self.close()
         except Exception:
             pass
+
+
+# ---------------------------------------------------------------------------
+# Philox4x32-10 (production RNG mode; no reference counterpart)
+# ---------------------------------------------------------------------------
+_PHILOX_M0, _PHILOX_M1 = 0xD2511F53, 0xCD9E8D57
+_PHILOX_W0, _PHILOX_W1 = 0x9E3779B9, 0xBB67AE85
+_M32 = 0xFFFFFFFF
+
+
+def philox4x32_10(ctr, key):
+    """Philox4x32 with 10 rounds, the published counter-based generator of
+    Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as easy as 1,
+    2, 3" (SC'11): per round, two 32x32->64 multiplies of counter words 0 and
+    2 by M0 / M1, the high halves XORed with the other counter words and the
+    key, the key bumped by the Weyl constants W0 / W1 between rounds.
+    ctr: 4 uint32, key: 2 uint32 -> 4 uint32."""
+    c0, c1, c2, c3 = (int(v) & _M32 for v in ctr)
+    k0, k1 = (int(v) & _M32 for v in key)
+    for _ in range(10):
+        p0 = _PHILOX_M0 * c0
+        p1 = _PHILOX_M1 * c2
+        hi0, lo0 = p0 >> 32, p0 & _M32
+        hi1, lo1 = p1 >> 32, p1 & _M32
+        c0, c1, c2, c3 = hi1 ^ c1 ^ k0, lo1, hi0 ^ c3 ^ k1, lo0
+        k0 = (k0 + _PHILOX_W0) & _M32
+        k1 = (k1 + _PHILOX_W1) & _M32
+    return c0, c1, c2, c3
+
+
+def philox_uniform(seed: int, offset: int, row: int) -> float:
+    """The uniform the library's u == NULL mode draws for `row`: Philox4x32-10
+    with key = seed (low word first) and counter = (row, 0, offset low,
+    offset high); the first two output words g1, g2 become
+    (g1 + g2 * 2^32) / 2^64 rounded once to double (the form
+    std::generate_canonical<double,53> gives two 32-bit draws), kept below 1."""
+    seed, offset = int(seed), int(offset)
+    g = philox4x32_10((row & _M32, 0, offset & _M32, (offset >> 32) & _M32), (seed & _M32, (seed >> 32) & _M32))
+    s = float(g[0]) + float(g[1]) * 4294967296.0
+    u = s * 5.421010862427522e-20
+    if u >= 1.0:
+        u = float(np.nextafter(1.0, 0.0))
+    return u
+
+
+def reference_root():
+    """The reference source tree, where it is present: $QWENIUM_REF, else a
+    `reference` directory beside this repository's checkout. None when
+    neither exists (the GPU box: the checker libraries travel prebuilt)."""
+    cand = os.environ.get("QWENIUM_REF") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isdir(os.path.join(cand, "src", "sampling")) else None

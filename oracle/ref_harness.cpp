@@ -200,8 +200,8 @@ int qwref_sampler_sample_full(int kind, float temperature, float rep_penalty, in
 }
 
 // Many rows through TemperatureSampler::sample, split over n_threads
-// std::threads with one sampler per row (the way BASELINE's CPU figure (ii)
-// runs the reference). Used to time the reference on the host cores.
+// std::threads with one sampler per row (rows spread over all host cores).
+// Used to time the reference on the host cores.
 int qwref_temperature_sample_batch(const float* logits, int B, int V, int64_t row_stride,
                                    const float* temperature, const int32_t* top_k,
                                    const float* top_p, const float* rep_penalty,

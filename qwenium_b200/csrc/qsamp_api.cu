@@ -95,6 +95,13 @@ struct qsamp_ctx {
     DevBuf<int> ready;
     DevBuf<unsigned long long> vparts;  // greedy verification: per-segment argmax keys
     int* pinned_one = nullptr;
+    // the device status word of the last asynchronous call, copied here in
+    // stream order at the end of the call (qsamp_poll_status reads it)
+    int* pinned_status = nullptr;
+    // device-side bounds (qsamp_set_limits)
+    int max_rounds = kMaxRounds;
+    unsigned long long ready_wait_ns = 1000000000ull;
+    int drop_ready_from = -1;
     size_t attrs_smem = 0;
     size_t max_dyn = 0;    // largest dynamic shared memory a CTA of the kernel may use
     qsamp_counters ctr = {};
@@ -275,18 +282,36 @@ qsamp_status ensure_luts(qsamp_ctx* c, const qsamp_batch* b, cudaStream_t st) {
     return QSAMP_OK;
 }
 
-qsamp_status read_status(qsamp_ctx* c) {
-    int st = 0;
-    cudaError_t e = cudaMemcpy(&st, c->status.p, sizeof(int), cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return cuda_fail(c, e, "reading the device status");
+// The kernels' status word (first error wins) as a qsamp_status.
+qsamp_status status_of(qsamp_ctx* c, int st) {
     switch (st) {
         case qs::DEV_OK: return QSAMP_OK;
         case qs::DEV_TOPK_TOO_LARGE: return fail(c, QSAMP_ERR_DEVICE, "device: top-k above the sorted-candidate limit");
         case qs::DEV_ROUNDS_EXHAUSTED:
             return fail(c, QSAMP_ERR_DEVICE,
-                        "device: a row needed more sorted elements than one gather round holds (token -1)");
+                        "device: a full-vocabulary row needed more gather rounds than allowed (max_rounds %d; token -1)",
+                        c->max_rounds);
+        case qs::DEV_TIMEOUT:
+            return fail(c, QSAMP_ERR_DEVICE,
+                        "device: a bounded wait ran out (row data did not arrive within %llu ns, or a slice copy did "
+                        "not complete; token -1)",
+                        c->ready_wait_ns);
         default: return fail(c, QSAMP_ERR_DEVICE, "device: internal status %d", st);
     }
+}
+
+qsamp_status read_status(qsamp_ctx* c) {
+    int st = 0;
+    cudaError_t e = cudaMemcpy(&st, c->status.p, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(c, e, "reading the device status");
+    *c->pinned_status = st;
+    return status_of(c, st);
+}
+
+// Stream-ordered copy of the status word for qsamp_poll_status.
+qsamp_status mirror_status(qsamp_ctx* c, cudaStream_t st) {
+    cudaError_t e = cudaMemcpyAsync(c->pinned_status, c->status.p, sizeof(int), cudaMemcpyDeviceToHost, st);
+    return e == cudaSuccess ? QSAMP_OK : cuda_fail(c, e, "copying the device status");
 }
 
 }  // namespace
@@ -319,6 +344,8 @@ qsamp_status qsamp_create(int32_t device, qsamp_ctx** out) {
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->copy_done, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaHostAlloc((void**)&c->pinned_one, sizeof(int), cudaHostAllocDefault);
     if (e == cudaSuccess) *c->pinned_one = 1;
+    if (e == cudaSuccess) e = cudaHostAlloc((void**)&c->pinned_status, sizeof(int), cudaHostAllocDefault);
+    if (e == cudaSuccess) *c->pinned_status = 0;
     cudaSetDevice(prev);
     if (e != cudaSuccess) {
         qsamp_destroy(c);  // releases whatever was created
@@ -352,6 +379,7 @@ void qsamp_destroy(qsamp_ctx* c) {
     c->ready.release();
     c->vparts.release();
     if (c->pinned_one) cudaFreeHost(c->pinned_one);
+    if (c->pinned_status) cudaFreeHost(c->pinned_status);
     if (c->copy_go) cudaEventDestroy(c->copy_go);
     if (c->copy_done) cudaEventDestroy(c->copy_done);
     if (c->copy) cudaStreamDestroy(c->copy);
@@ -422,7 +450,8 @@ static qsamp_status common_setup(qsamp_ctx* c, const qsamp_batch* b, cudaStream_
     a.status = c->status.p;
     a.row_ctr = c->status.p + 1;
     a.srow_ctr = c->status.p + 2;
-    a.max_rounds = kMaxRounds;
+    a.max_rounds = c->max_rounds;
+    a.ready_wait_ns = c->ready_wait_ns;
     return QSAMP_OK;
 }
 
@@ -441,6 +470,8 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     a.ready = ready;
     a.ready_rows = ready_rows;
     for (bool& u : c->ev_used) u = false;
+    c->ctr.last_cluster_size = 0;
+    c->ctr.last_clusters = 0;
 
     // Route rows: greedy rows and top-k rows (k <= 1024) with a penalty
     // window of at most 1024 ids stream through one CTA each; the rest (full
@@ -522,6 +553,8 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         ca.rows = c->rows.p + n_stream;
         ca.nrows = n_cluster;
         ca.n_s = plan.n_s;
+        c->ctr.last_cluster_size = plan.cl;
+        c->ctr.last_clusters = plan.clusters;
         t_begin(c, T_ROWS, st);
         e = qs_launch_rows(&ca, plan.clusters, plan.cl, plan.smem, st);
         if (e != cudaSuccess) return cuda_fail(c, e, "selection kernel launch");
@@ -551,7 +584,9 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     c->ctr.calls += 1;
     c->ctr.rows += (uint64_t)B;
     c->ctr.logit_bytes += (uint64_t)B * (uint64_t)b->V * esz;
-    return QSAMP_OK;
+    c->ctr.last_stream_rows = n_stream;
+    c->ctr.last_cluster_rows = n_cluster;
+    return mirror_status(c, st);
 }
 
 qsamp_status qsamp_sample(qsamp_ctx* c, const qsamp_batch* b, void* stream) {
@@ -612,7 +647,9 @@ qsamp_status qsamp_sample_host(qsamp_ctx* c, const qsamp_batch* hb) {
                                       (const unsigned char*)hb->logits + (size_t)r0 * hb->row_stride * esz,
                                       (size_t)hb->row_stride * esz, (size_t)V * esz, (size_t)nr,
                                       cudaMemcpyHostToDevice, c->copy);
-                if (e == cudaSuccess)
+                // (fault injection for tests: chunks from drop_ready_from on
+                // never raise their flag)
+                if (e == cudaSuccess && (c->drop_ready_from < 0 || j < c->drop_ready_from))
                     e = cudaMemcpyAsync(c->ready.p + j, c->pinned_one, sizeof(int), cudaMemcpyHostToDevice, c->copy);
             }
             if (e != cudaSuccess) break;
@@ -682,6 +719,37 @@ qsamp_status qsamp_sample_host(qsamp_ctx* c, const qsamp_batch* hb) {
         std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count();
     if (prev != c->device) cudaSetDevice(prev);
     return s;
+}
+
+qsamp_status qsamp_poll_status(qsamp_ctx* c) {
+    if (!c) return QSAMP_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> g(c->mu);
+    return status_of(c, *(volatile int*)c->pinned_status);
+}
+
+qsamp_status qsamp_set_limits(qsamp_ctx* c, const qsamp_limits* l) {
+    if (!c) return QSAMP_ERR_INVALID_ARG;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (!l) return fail(c, QSAMP_ERR_INVALID_ARG, "limits: expected non-NULL");
+    if (l->max_rounds < 1)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "limits.max_rounds: expected >= 1, got %d", l->max_rounds);
+    if (l->ready_wait_ns < 1000)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "limits.ready_wait_ns: expected >= 1000, got %lld",
+                    (long long)l->ready_wait_ns);
+    if (l->drop_ready_from < -1)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "limits.drop_ready_from: expected >= -1, got %d", l->drop_ready_from);
+    c->max_rounds = l->max_rounds;
+    c->ready_wait_ns = (unsigned long long)l->ready_wait_ns;
+    c->drop_ready_from = l->drop_ready_from;
+    return QSAMP_OK;
+}
+
+qsamp_status qsamp_get_limits(const qsamp_ctx* c, qsamp_limits* out) {
+    if (!c || !out) return QSAMP_ERR_INVALID_ARG;
+    out->max_rounds = c->max_rounds;
+    out->ready_wait_ns = (int64_t)c->ready_wait_ns;
+    out->drop_ready_from = c->drop_ready_from;
+    return QSAMP_OK;
 }
 
 qsamp_status qsamp_get_counters(const qsamp_ctx* c, qsamp_counters* out) {
@@ -939,7 +1007,7 @@ static qsamp_status shard_locked(qsamp_ctx* c, const qsamp_batch* lb, int32_t v_
     c->ctr.calls += 1;
     c->ctr.rows += (uint64_t)B;
     c->ctr.logit_bytes += (uint64_t)B * (uint64_t)lb->V * (lb->dtype == QSAMP_BF16 ? 2 : 4);
-    return QSAMP_OK;
+    return mirror_status(c, st);
 }
 
 qsamp_status qsamp_shard_topk(qsamp_ctx* c, const qsamp_batch* lb, int32_t v_offset, int32_t V_total, int32_t k,
@@ -1013,7 +1081,7 @@ static qsamp_status merge_locked(qsamp_ctx* c, int32_t n_ranks, int32_t B, int32
     if ((e = qs_launch_merge(&a, all_vals, all_ids, n_ranks, k, grid, smem, st)) != cudaSuccess)
         return cuda_fail(c, e, "merge kernel launch");
     t_end(c, T_MERGE, st);
-    return QSAMP_OK;
+    return mirror_status(c, st);
 }
 
 qsamp_status qsamp_merge_topk(qsamp_ctx* c, int32_t n_ranks, int32_t B, int32_t k, const float* all_vals,

@@ -68,6 +68,7 @@ struct QsLaunch {
     // once ready[r / ready_rows] != 0; null: all rows are resident at launch
     const int* ready;
     int ready_rows;
+    unsigned long long ready_wait_ns;  // longest wait for one ready flag
 };
 
 // Dynamic shared-memory layout; identical on host (sizing) and device.
@@ -94,6 +95,8 @@ struct __align__(16) Misc {
     int sel_rem;           // broadcast remaining rank
     int sel_cnt;           // broadcast count of the chosen bin
     int next_ri;           // leading CTA: the cluster's next row-list entry
+    int skip;              // this CTA's row data did not arrive in time (wait ran out)
+    int skip_row;          // some CTA of the cluster skips the row: token -1
     unsigned long long sel_remw;  // broadcast remaining weight (weighted select)
     float S_n, S_c;        // exact sums (broadcast)
     int first_round;

@@ -876,22 +876,45 @@ __device__ bool slice_bar_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
-__device__ void wait_ready(const QsLaunch& a, int row) {
-    if (!a.ready) return;
+// Returns false (and sets DEV_TIMEOUT) when the flag stayed clear for
+// a.ready_wait_ns; every thread of the CTA gets the same answer. On success
+// the bulk copies that follow (async proxy) are ordered after the acquire of
+// the flag that published the row's bytes.
+__device__ bool wait_ready(const QsLaunch& a, int row) {
+    if (!a.ready) return true;
+    __shared__ int ready_ok;
     if (threadIdx.x == 0) {
         const int* f = a.ready + row / a.ready_rows;
-        for (int it = 0;; ++it) {
+        unsigned long long t0, t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        int ok = 0;
+        while (true) {
             int v;
             asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-            if (v != 0) break;
-            if (it >= (1 << 24)) {
-                set_status(a.status, DEV_TIMEOUT);
+            if (v != 0) {
+                ok = 1;
                 break;
             }
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            if (t - t0 > a.ready_wait_ns) break;
             __nanosleep(200);
         }
+        if (ok) asm volatile("fence.proxy.async.global;" ::: "memory");
+        else set_status(a.status, DEV_TIMEOUT);
+        ready_ok = ok;
     }
     __syncthreads();
+    return ready_ok != 0;
+}
+
+// The result of a row whose data did not arrive in time (or whose slice copy
+// did not complete): token -1, position -1; no draw.
+__device__ void write_skipped(const QsLaunch& a, int row) {
+    qsamp_row_result res = {};
+    res.token = -1;
+    res.position = -1;
+    a.results[row] = res;
+    if (a.out_ids) a.out_ids[row] = -1;
 }
 
 __device__ void write_result(const QsLaunch& a, int row, const qsamp_row_result& res) {
@@ -2519,9 +2542,13 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
                 if (a.lut_caps[q] == p.softcap) r.lut = a.luts + (size_t)q * 65536;
         }
 
-        wait_ready(a, row);
+        // a row whose data does not arrive in time is skipped by the whole
+        // cluster (token -1): each CTA records its own outcome here, and the
+        // cluster reads every CTA's after the barrier that follows the transform
+        const bool arrived = wait_ready(a, row);
+        if (threadIdx.x == 0) m->skip = arrived ? 0 : 1;
         // fp32 slices: the bulk copy runs while the penalty table is built
-        const bool insm = a.dtype != QSAMP_BF16 && a.vec_ok && !r.force_on && r.len >= 8;
+        const bool insm = arrived && a.dtype != QSAMP_BF16 && a.vec_ok && !r.force_on && r.len >= 8;
         if (insm && threadIdx.x == 0)
             slice_bulk_load(s.vals, (const float*)r.rowp + r.lo, (uint32_t)(r.len / 4) * 16u, &slice_bar);
         QS_TMARK(row, 0, rank == 0);
@@ -2532,12 +2559,19 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
         uint32_t* pbits = (uint32_t*)s.gs;
         const PenWin pw = penalty_table(r, a, s, pbits);
         QS_TMARK(row, 1, rank == 0);
+        bool copy_lost = false;
         if (insm) {
             if (!slice_bar_wait(&slice_bar, slice_par)) {
                 // (not expected: the copy reads this row's own bytes) report it,
-                // and wait once more so that no copy is still in flight
-                if (threadIdx.x == 0) set_status(a.status, DEV_TIMEOUT);
-                slice_bar_wait(&slice_bar, slice_par);
+                // skip the row, and wait once more so that no copy is still in
+                // flight; if that wait also runs out the cluster stops serving
+                // rows (its shared memory may still be written)
+                if (threadIdx.x == 0) {
+                    set_status(a.status, DEV_TIMEOUT);
+                    m->skip = 1;
+                }
+                copy_lost = !slice_bar_wait(&slice_bar, slice_par);
+                if (copy_lost && threadIdx.x == 0) m->skip = 2;
             }
             slice_par ^= 1u;
         }
@@ -2556,23 +2590,50 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
             // largest value, lowest id among equals
             float gm = NEG_INF;
             int gi = 0x7fffffff;
+            int sk = 0;
             for (int q = threadIdx.x; q < CL; q += 32) {
                 const Misc* pm = peer(cl, m, q);
                 const float v = pm->cmax;
                 const int i = pm->cmax_idx;
+                sk = max(sk, pm->skip);
                 if (v > gm || (v == gm && i < gi)) { gm = v; gi = i; }
             }
             for (int o = 16; o > 0; o >>= 1) {
                 const float v = __shfl_down_sync(FULLMASK, gm, o);
                 const int i = __shfl_down_sync(FULLMASK, gi, o);
+                sk = max(sk, __shfl_down_sync(FULLMASK, sk, o));
                 if (v > gm || (v == gm && i < gi)) { gm = v; gi = i; }
             }
             if (threadIdx.x == 0) {
                 m->M = gm;
                 m->argmax = gi == 0x7fffffff ? 0 : gi;
+                m->skip_row = sk;
             }
         }
         __syncthreads();
+        if (m->skip_row) {
+            if (rank == 0) {
+                if (threadIdx.x == 0) write_skipped(a, row);
+                if (a.top_ids)
+                    for (int i = threadIdx.x; i < a.top_cap; i += NT) {
+                        a.top_ids[(size_t)row * a.top_cap + i] = -1;
+                        a.top_probs[(size_t)row * a.top_cap + i] = 0.0f;
+                    }
+            }
+            // a slice copy that never completed may still write this CTA's
+            // shared memory: every CTA of the cluster leaves together (after
+            // the barrier, so that no peer reads a departed CTA)
+            const bool stop = m->skip_row >= 2;
+            cl.sync();
+            if (stop) return;
+            if (a.row_ctr && rank == 0 && threadIdx.x == 0) {
+                const int nx = ncl + atomicAdd(a.row_ctr, 1);
+                for (int q = 0; q < CL; ++q) peer(cl, &m->next_ri, q)[0] = nx;
+            }
+            cl.sync();
+            ri = a.row_ctr ? m->next_ri : ri + ncl;
+            continue;
+        }
 
         const float M = m->M;
         const int V = a.V;
@@ -2993,7 +3054,28 @@ __global__ void __launch_bounds__(SN_NT, 2) qs_stream_kernel(QsLaunch a) {
     __shared__ int sn_next;
     for (int ri = blockIdx.x; ri < a.nrows;) {
         const int row = a.rows[ri];
-        wait_ready(a, row);
+        if (!wait_ready(a, row)) {
+            // the row's data did not arrive in time: token -1 (candidates:
+            // padding only), and on to the next row
+            if (a.cand_vals) {
+                for (int i = threadIdx.x; i < a.cand_k; i += SN_NT) {
+                    a.cand_vals[(size_t)row * a.cand_k + i] = NEG_INF;
+                    a.cand_ids[(size_t)row * a.cand_k + i] = -1;
+                }
+            } else {
+                if (threadIdx.x == 0) write_skipped(a, row);
+                if (a.top_ids)
+                    for (int i = threadIdx.x; i < a.top_cap; i += SN_NT) {
+                        a.top_ids[(size_t)row * a.top_cap + i] = -1;
+                        a.top_probs[(size_t)row * a.top_cap + i] = 0.0f;
+                    }
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) sn_next = a.srow_ctr ? (int)gridDim.x + atomicAdd(a.srow_ctr, 1) : ri + (int)gridDim.x;
+            __syncthreads();
+            ri = sn_next;
+            continue;
+        }
         QS_TMARK(row, 0, true);
         if (threadIdx.x == 0) { m->prm = a.params[row]; sh_nuniq = 0; sh_n = 0; sh_tau = 0ull; sh_xthr = -__int_as_float(0x7f800000); }
         __syncthreads();

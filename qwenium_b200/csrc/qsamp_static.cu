@@ -2,11 +2,11 @@
 // device allocation.
 //
 // Who needs it: callers that cannot allocate device memory at the point
-// where they sample -- code running while a CUDA graph is being captured by
-// someone else's allocator rules, a serving engine whose device memory is
-// fully reserved up front, or a plugin host that forbids its plugins to call
-// cudaMalloc. qsamp_create() allocates (its scratch buffers and a stream), so
-// those callers cannot hold a qsamp_ctx; this entry point needs none.
+// where they sample -- a serving engine whose device memory is fully
+// reserved up front by its own allocator, or a plugin host that forbids its
+// plugins to call cudaMalloc. qsamp_create() allocates (its scratch buffers
+// and a stream), so those callers cannot hold a qsamp_ctx; this entry point
+// needs none.
 //
 // Where the scratch lives instead: qs_static_scratch below, a file-scope
 // __device__ array of QSAMP_STATIC_SCRATCH_BYTES (640 KiB). Every GPU

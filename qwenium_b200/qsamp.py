@@ -64,6 +64,7 @@ EXPORTS = (
     "qsamp_pack_ids", "qsamp_grammar_mask", "qsamp_find_eos_string", "qsamp_keep_list_mask",
     "qsamp_mask_and", "qsamp_shard_topk", "qsamp_merge_topk", "qsamp_get_counters", "qsamp_set_kernel_timing",
     "qsamp_sample_static", "qsamp_first_byte_table", "qsamp_char_class_masks", "qsamp_verify_greedy",
+    "qsamp_poll_status", "qsamp_set_limits", "qsamp_get_limits",
 )
 
 _P = ctypes.c_void_p
@@ -109,6 +110,18 @@ class _Counters(ctypes.Structure):
         ("last_stream_kernel_ms", ctypes.c_double),
         ("last_rows_kernel_ms", ctypes.c_double),
         ("last_merge_kernel_ms", ctypes.c_double),
+        ("last_stream_rows", ctypes.c_int32),
+        ("last_cluster_rows", ctypes.c_int32),
+        ("last_cluster_size", ctypes.c_int32),
+        ("last_clusters", ctypes.c_int32),
+    ]
+
+
+class _Limits(ctypes.Structure):
+    _fields_ = [
+        ("max_rounds", ctypes.c_int32),
+        ("drop_ready_from", ctypes.c_int32),
+        ("ready_wait_ns", ctypes.c_int64),
     ]
 
 
@@ -164,6 +177,12 @@ def load(path: str = LIB_PATH):
     lib.qsamp_set_kernel_timing.argtypes = [_P, ctypes.c_int32]
     lib.qsamp_sample_static.restype = ctypes.c_int
     lib.qsamp_sample_static.argtypes = [ctypes.POINTER(_Batch), _P, ctypes.c_char_p, ctypes.c_size_t]
+    lib.qsamp_poll_status.restype = ctypes.c_int
+    lib.qsamp_poll_status.argtypes = [_P]
+    lib.qsamp_set_limits.restype = ctypes.c_int
+    lib.qsamp_set_limits.argtypes = [_P, ctypes.POINTER(_Limits)]
+    lib.qsamp_get_limits.restype = ctypes.c_int
+    lib.qsamp_get_limits.argtypes = [_P, ctypes.POINTER(_Limits)]
     _lib = lib
     return lib
 
@@ -295,6 +314,26 @@ class Context:
     def set_kernel_timing(self, on: bool):
         """Bracket each selection kernel with CUDA events (see counters())."""
         self._check(self.lib.qsamp_set_kernel_timing(self.h, 1 if on else 0), "qsamp_set_kernel_timing")
+
+    def poll_status(self) -> None:
+        """qsamp_poll_status: raises QsampError (DEVICE) when the last
+        asynchronous call's kernels hit a device-side limit; call it after
+        synchronising that call's stream."""
+        self._check(self.lib.qsamp_poll_status(self.h), "qsamp_poll_status")
+
+    def limits(self) -> dict:
+        lim = _Limits()
+        self._check(self.lib.qsamp_get_limits(self.h, ctypes.byref(lim)), "qsamp_get_limits")
+        return {f: getattr(lim, f) for f, _ in lim._fields_}
+
+    def set_limits(self, max_rounds=None, ready_wait_ns=None, drop_ready_from=None) -> None:
+        """qsamp_set_limits; arguments left None keep their current value."""
+        cur = self.limits()
+        lim = _Limits()
+        lim.max_rounds = cur["max_rounds"] if max_rounds is None else int(max_rounds)
+        lim.ready_wait_ns = cur["ready_wait_ns"] if ready_wait_ns is None else int(ready_wait_ns)
+        lim.drop_ready_from = cur["drop_ready_from"] if drop_ready_from is None else int(drop_ready_from)
+        self._check(self.lib.qsamp_set_limits(self.h, ctypes.byref(lim)), "qsamp_set_limits")
 
     def verify_greedy(self, logits, row_off, drafts, eos_token: int = -1, stream=None):
         """qsamp_verify_greedy on CUDA tensors: logits [n_rows][V] (fp32, or
@@ -440,8 +479,10 @@ class Context:
         return out_results
 
     def sample_host(self, logits: np.ndarray, params, hist=None, hist_len=None, masks=None, u=None, rng_offset=0,
-                    top_cap=0, bf16=False):
-        """Host-memory entry (qsamp_sample_host): numpy in, numpy out."""
+                    top_cap=0, bf16=False, status_out=None):
+        """Host-memory entry (qsamp_sample_host): numpy in, numpy out.
+        With status_out (a list), a device-side status (QSAMP_ERR_DEVICE) is
+        appended to it instead of raised, and the outputs are returned."""
         logits = np.ascontiguousarray(logits)
         B, V = logits.shape
         params = np.ascontiguousarray(params, ROW_PARAMS)
@@ -464,7 +505,11 @@ class Context:
         b = self._batch(_np_ptr(logits), QSAMP_BF16 if bf16 else QSAMP_F32, B, V, V, params, hist_ptr, hstride,
                         hist_len, mptr, mstride, u, rng_offset, _np_ptr(ids), _np_ptr(res), _np_ptr(top_ids),
                         _np_ptr(top_probs), top_cap)
-        self._check(self.lib.qsamp_sample_host(self.h, ctypes.byref(b)), "qsamp_sample_host")
+        rc = self.lib.qsamp_sample_host(self.h, ctypes.byref(b))
+        if status_out is not None and rc == 4:
+            status_out.append((rc, self.lib.qsamp_last_error(self.h).decode(errors="replace")))
+        else:
+            self._check(rc, "qsamp_sample_host")
         return ids, res, top_ids, top_probs
 
 

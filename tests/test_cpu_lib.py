@@ -93,9 +93,11 @@ def test_adapter_compiles_against_reference_headers(tmp_path):
     it must compile against the reference's own src/sampling headers."""
     import subprocess
 
-    inc = "/root/reference/src/sampling"
-    if not os.path.exists(os.path.join(inc, "sampling.h")):
+    import oracle as O
+
+    if not O.reference_root():
         pytest.skip("reference headers not present")
+    inc = os.path.join(O.reference_root(), "src", "sampling")
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     r = subprocess.run(["g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-I", inc, "-I", os.path.join(root, "include"),
                         "-c", os.path.join(root, "qwenium_b200", "adapter", "cuda_sampler.cpp"),
