@@ -13,7 +13,9 @@
 // greedy, a pruning keep-set, a JSON grammar walk (GBNF text from argv[1]),
 // and empty logits (both throw). Prints one line per case; exit 0 iff all
 // agree. Built by oracle/Makefile into oracle/_ref/adapter_check.
+#include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -105,11 +107,57 @@ std::vector<std::string> grammar_vocab(int V) {
     return v;
 }
 
+// --time N: per-call latency of the drop-in samplers and of the reference's,
+// one row per call as Sampler::sample is called (C1: V=151936 logits ~N(0,3^2)
+// plus 20 ids boosted by +8, a 64-id history, repetition penalty 1.1 over 64;
+// T 0.8, top-k 40, top-p 0.95, and GreedySampler's defaults). Prints one
+// JSON object of mean milliseconds per call.
+template <typename S>
+double time_calls(S& s, const std::vector<std::vector<float>>& rows, const std::vector<int32_t>& hist, int n) {
+    const std::vector<std::string> none;
+    volatile int sink = 0;
+    auto t0 = std::chrono::steady_clock::now();
+    for (int i = 0; i < n; ++i) {
+        std::vector<float> x = rows[(size_t)i % rows.size()];
+        sink = sink + s.sample(x, hist, none);
+    }
+    const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    return ms / n;
+}
+
+int time_mode(int n) {
+    const int V = 151936;
+    std::vector<std::vector<float>> rows;
+    for (uint32_t r = 0; r < 4; ++r) {
+        std::vector<float> x = make_logits(700 + r, V, 3.0f);
+        std::mt19937 g(800 + r);
+        std::uniform_int_distribution<int> id(0, V - 1);
+        for (int j = 0; j < 20; ++j) x[(size_t)id(g)] += 8.0f;
+        rows.push_back(std::move(x));
+    }
+    std::vector<int32_t> hist;
+    std::mt19937 g(900);
+    std::uniform_int_distribution<int> id(0, V - 1);
+    for (int j = 0; j < 64; ++j) hist.push_back(id(g));
+    qwenium_b200::CudaTemperatureSampler ct(0.8f, 1.1f, 64, 40, 0.95f);
+    qwenium_b200::CudaGreedySampler cg;
+    qwenium::TemperatureSampler rt(0.8f, 1.1f, 64, 40, 0.95f);
+    qwenium::GreedySampler rg;
+    time_calls(ct, rows, hist, 3);  // context creation and first-call set-up
+    time_calls(cg, rows, hist, 3);
+    const double a = time_calls(ct, rows, hist, n), b = time_calls(cg, rows, hist, n);
+    const double c = time_calls(rt, rows, hist, n < 20 ? n : 20), d = time_calls(rg, rows, hist, n);
+    std::printf("{\"calls\": %d, \"cuda_temperature_ms\": %.4f, \"cuda_greedy_ms\": %.4f, "
+                "\"reference_temperature_ms\": %.4f, \"reference_greedy_ms\": %.4f}\n", n, a, b, c, d);
+    return 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
     const int V = 151936;
     const std::vector<std::string> none;
+    if (argc > 2 && std::strcmp(argv[1], "--time") == 0) return time_mode(std::atoi(argv[2]));
     try {
         {  // full vocabulary, top-p only
             qwenium::TemperatureSampler ref(1.0f, 1.1f, 64, 0, 0.9f);
