@@ -219,6 +219,33 @@ qsamp_status qsamp_char_class_masks(qsamp_ctx* ctx, const uint16_t* table, int32
                                     const uint32_t* classes, uint32_t* masks, int64_t mask_stride, int32_t or_into,
                                     void* stream);
 
+/* Compact token trie (host). ----------------------------------------------
+ * The queries of the reference's qwenium::TokenTrie (token-trie.h:20-64,
+ * token-trie.cpp:8-126) with identical results in identical order, over a
+ * flat sorted-string representation instead of 256-pointer nodes
+ * (token-trie.h:11-16). C++ callers use qwenium_b200/trie/token-trie.h,
+ * a drop-in qwenium::TokenTrie; this is the C ABI over the same code.
+ * qsamp_trie_build: token i is strs[i] (lens[i] bytes); empty tokens are
+ * skipped (token-trie.cpp:18). The collect functions write at most cap ids
+ * into out and return how many the query yields (-1: invalid argument):
+ *   by_prefix     collect_by_prefix(prefix[0:len], offset)  (token-trie.cpp:39-70)
+ *   by_char_class collect_by_char_class(set of chars[0:n], negated)  (:72-84)
+ *   by_first_char collect_by_first_char(c)  (:86-91)
+ * qsamp_trie_mark_char_class sets mask_out[i] = 1 for the marked tokens and
+ * 0 elsewhere (mark_char_class, :93-116); V must cover every marked id. */
+typedef struct qsamp_trie qsamp_trie;
+qsamp_status qsamp_trie_build(const char* const* strs, const int32_t* lens, int32_t V, qsamp_trie** out);
+void qsamp_trie_free(qsamp_trie* trie);
+int64_t qsamp_trie_token_count(const qsamp_trie* trie);
+int64_t qsamp_trie_memory_bytes(const qsamp_trie* trie);
+int64_t qsamp_trie_collect_by_prefix(const qsamp_trie* trie, const char* prefix, int32_t len, int32_t offset,
+                                     int32_t* out, int64_t cap);
+int64_t qsamp_trie_collect_by_char_class(const qsamp_trie* trie, const uint8_t* chars, int32_t n, int32_t negated,
+                                         int32_t* out, int64_t cap);
+int64_t qsamp_trie_collect_by_first_char(const qsamp_trie* trie, uint8_t c, int32_t* out, int64_t cap);
+qsamp_status qsamp_trie_mark_char_class(const qsamp_trie* trie, const uint8_t* chars, int32_t n, int32_t negated,
+                                        int32_t V, uint8_t* mask_out);
+
 /* Vocab-sharded selection (tensor-parallel output head). No counterpart in
  * the reference (its sampler sees whole rows). ----------------------------
  * Rank r holds logits[:, v_offset : v_offset + V_local] of a V_total vocab

@@ -137,6 +137,15 @@ def ref_lib(kind: str = "strict"):
         lib.qwref_spec_verify.argtypes = [_P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P, _P]
         lib.qwref_trie_mark_char_class.restype = None
         lib.qwref_trie_mark_char_class.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P]
+        lib.qwref_trie_collect_by_prefix.restype = ctypes.c_int
+        lib.qwref_trie_collect_by_prefix.argtypes = [_P, ctypes.c_char_p, ctypes.c_int, ctypes.c_int, _P,
+                                                     ctypes.c_int]
+        lib.qwref_trie_collect_by_char_class.restype = ctypes.c_int
+        lib.qwref_trie_collect_by_char_class.argtypes = [_P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int]
+        lib.qwref_trie_collect_by_first_char.restype = ctypes.c_int
+        lib.qwref_trie_collect_by_first_char.argtypes = [_P, ctypes.c_uint8, _P, ctypes.c_int]
+        lib.qwref_trie_token_count.restype = ctypes.c_longlong
+        lib.qwref_trie_token_count.argtypes = [_P]
         lib.qwref_sampler_sample_full.restype = ctypes.c_int
         lib.qwref_sampler_sample_full.argtypes = [
             ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_float,

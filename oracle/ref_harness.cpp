@@ -160,6 +160,35 @@ void qwref_trie_mark_char_class(void* trie, const unsigned char* chars, int n, i
     for (int i = 0; i < V; ++i) out[i] = mask[static_cast<size_t>(i)] ? 1 : 0;
 }
 
+// TokenTrie::collect_by_prefix / collect_by_char_class / collect_by_first_char
+// (token-trie.cpp:39-91): the ids in the reference's order; at most cap are
+// written, the full count is returned.
+static int emit_ids(const std::vector<int32_t>& v, int32_t* out, int cap) {
+    for (size_t i = 0; i < v.size() && (int)i < cap; ++i) out[i] = v[i];
+    return (int)v.size();
+}
+int qwref_trie_collect_by_prefix(void* trie, const char* prefix, int len, int offset, int32_t* out, int cap) {
+    std::vector<int32_t> v;
+    static_cast<qwenium::TokenTrie*>(trie)->collect_by_prefix(std::string(prefix, (size_t)len), (size_t)offset, v);
+    return emit_ids(v, out, cap);
+}
+int qwref_trie_collect_by_char_class(void* trie, const unsigned char* chars, int n, int negated, int32_t* out,
+                                     int cap) {
+    std::set<char> cs;
+    for (int i = 0; i < n; ++i) cs.insert(static_cast<char>(chars[i]));
+    std::vector<int32_t> v;
+    static_cast<qwenium::TokenTrie*>(trie)->collect_by_char_class(cs, negated != 0, v);
+    return emit_ids(v, out, cap);
+}
+int qwref_trie_collect_by_first_char(void* trie, unsigned char c, int32_t* out, int cap) {
+    std::vector<int32_t> v;
+    static_cast<qwenium::TokenTrie*>(trie)->collect_by_first_char(static_cast<char>(c), v);
+    return emit_ids(v, out, cap);
+}
+long long qwref_trie_token_count(void* trie) {
+    return (long long)static_cast<qwenium::TokenTrie*>(trie)->token_count();
+}
+
 // The full Sampler::sample path with a grammar, an EOS id and/or a pruning
 // keep-set attached (sampling.cpp:12-81): exercises apply_vocab_pruning,
 // apply_grammar_constraints (EOS allowance, stuck-grammar EOS forcing) and

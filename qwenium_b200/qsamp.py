@@ -65,6 +65,9 @@ EXPORTS = (
     "qsamp_mask_and", "qsamp_shard_topk", "qsamp_merge_topk", "qsamp_get_counters", "qsamp_set_kernel_timing",
     "qsamp_sample_static", "qsamp_first_byte_table", "qsamp_char_class_masks", "qsamp_verify_greedy",
     "qsamp_poll_status", "qsamp_set_limits", "qsamp_get_limits",
+    "qsamp_trie_build", "qsamp_trie_free", "qsamp_trie_token_count", "qsamp_trie_memory_bytes",
+    "qsamp_trie_collect_by_prefix", "qsamp_trie_collect_by_char_class", "qsamp_trie_collect_by_first_char",
+    "qsamp_trie_mark_char_class",
 )
 
 _P = ctypes.c_void_p
@@ -183,6 +186,22 @@ def load(path: str = LIB_PATH):
     lib.qsamp_set_limits.argtypes = [_P, ctypes.POINTER(_Limits)]
     lib.qsamp_get_limits.restype = ctypes.c_int
     lib.qsamp_get_limits.argtypes = [_P, ctypes.POINTER(_Limits)]
+    lib.qsamp_trie_build.restype = ctypes.c_int
+    lib.qsamp_trie_build.argtypes = [_P, _P, ctypes.c_int32, ctypes.POINTER(_P)]
+    lib.qsamp_trie_free.restype = None
+    lib.qsamp_trie_free.argtypes = [_P]
+    for f in ("qsamp_trie_token_count", "qsamp_trie_memory_bytes"):
+        getattr(lib, f).restype = ctypes.c_int64
+        getattr(lib, f).argtypes = [_P]
+    lib.qsamp_trie_collect_by_prefix.restype = ctypes.c_int64
+    lib.qsamp_trie_collect_by_prefix.argtypes = [_P, ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32, _P,
+                                                 ctypes.c_int64]
+    lib.qsamp_trie_collect_by_char_class.restype = ctypes.c_int64
+    lib.qsamp_trie_collect_by_char_class.argtypes = [_P, _P, ctypes.c_int32, ctypes.c_int32, _P, ctypes.c_int64]
+    lib.qsamp_trie_collect_by_first_char.restype = ctypes.c_int64
+    lib.qsamp_trie_collect_by_first_char.argtypes = [_P, ctypes.c_uint8, _P, ctypes.c_int64]
+    lib.qsamp_trie_mark_char_class.restype = ctypes.c_int
+    lib.qsamp_trie_mark_char_class.argtypes = [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P]
     _lib = lib
     return lib
 
@@ -644,3 +663,79 @@ def sample_static(logits, params, hist=None, hist_len=None, masks=None, u=None, 
     rc = lib.qsamp_sample_static(ctypes.byref(b), ctypes.c_void_p(stream), err, len(err))
     if rc:
         raise QsampError(rc, "qsamp_sample_static: " + err.value.decode(errors="replace"))
+
+
+# ---------------------------------------------------------------- compact token trie
+class TokenTrie:
+    """The reference's TokenTrie queries (src/sampling/token-trie.h:20-64) over
+    the library's compact trie (qsamp_trie_*): build(vocab), then
+    collect_by_prefix / collect_by_char_class / collect_by_first_char return
+    id arrays in the reference's order, mark_char_class a bool array."""
+
+    def __init__(self, vocab: Optional[Sequence] = None):
+        self.lib = load()
+        self.h = None
+        self.V = 0
+        if vocab is not None:
+            self.build(vocab)
+
+    def build(self, vocab: Sequence) -> None:
+        self.close()
+        bs = [s.encode("latin-1") if isinstance(s, str) else bytes(s) for s in vocab]
+        bufs = [ctypes.create_string_buffer(b, len(b) + 1) for b in bs]
+        arr = (ctypes.c_void_p * len(bs))(*[ctypes.addressof(b) for b in bufs])
+        lens = np.array([len(b) for b in bs], np.int32)
+        h = _P()
+        rc = self.lib.qsamp_trie_build(ctypes.cast(arr, _P), _np_ptr(lens), len(bs), ctypes.byref(h))
+        if rc:
+            raise QsampError(rc, "qsamp_trie_build")
+        self.h = h
+        self.V = len(bs)
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.qsamp_trie_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def token_count(self) -> int:
+        return int(self.lib.qsamp_trie_token_count(self.h))
+
+    def memory_bytes(self) -> int:
+        return int(self.lib.qsamp_trie_memory_bytes(self.h))
+
+    def _collect(self, fn, *args) -> np.ndarray:
+        n = fn(self.h, *args, None, 0)
+        if n < 0:
+            raise QsampError(1, "qsamp_trie query: invalid argument")
+        out = np.empty(max(n, 1), np.int32)
+        fn(self.h, *args, _np_ptr(out), n)
+        return out[:n]
+
+    def collect_by_prefix(self, prefix, offset: int = 0) -> np.ndarray:
+        b = prefix.encode("latin-1") if isinstance(prefix, str) else bytes(prefix)
+        return self._collect(self.lib.qsamp_trie_collect_by_prefix, b, len(b), int(offset))
+
+    @staticmethod
+    def _chars(chars) -> np.ndarray:
+        return np.array([c if isinstance(c, (int, np.integer)) else ord(c) for c in chars], np.uint8)
+
+    def collect_by_char_class(self, chars, negated: bool) -> np.ndarray:
+        c = self._chars(chars)
+        return self._collect(self.lib.qsamp_trie_collect_by_char_class, _np_ptr(c), c.size, int(bool(negated)))
+
+    def collect_by_first_char(self, c) -> np.ndarray:
+        return self._collect(self.lib.qsamp_trie_collect_by_first_char, int(c if isinstance(c, int) else ord(c)))
+
+    def mark_char_class(self, chars, negated: bool) -> np.ndarray:
+        c = self._chars(chars)
+        out = np.zeros(self.V, np.uint8)
+        rc = self.lib.qsamp_trie_mark_char_class(self.h, _np_ptr(c), c.size, int(bool(negated)), self.V, _np_ptr(out))
+        if rc:
+            raise QsampError(rc, "qsamp_trie_mark_char_class")
+        return out.astype(bool)
