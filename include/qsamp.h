@@ -135,11 +135,16 @@ qsamp_status qsamp_poll_status(qsamp_ctx* ctx);
  *   drop_ready_from fault injection for tests: chunks with index >= this
  *                   value never raise their arrival flag (their bytes are
  *                   still copied), so the kernels' bounded waits run out;
- *                   -1 (the default) turns it off. */
+ *                   -1 (the default) turns it off.
+ *   hist_path       1 (the default): bf16 rows with a full-vocabulary top-p
+ *                   take the histogram kernel; 0: the cluster kernel serves
+ *                   them (both give the same rows bit for bit). */
 typedef struct qsamp_limits {
     int32_t max_rounds;
     int32_t drop_ready_from;
     int64_t ready_wait_ns;
+    int32_t hist_path;
+    int32_t reserved;
 } qsamp_limits;
 qsamp_status qsamp_set_limits(qsamp_ctx* ctx, const qsamp_limits* limits);
 qsamp_status qsamp_get_limits(const qsamp_ctx* ctx, qsamp_limits* out);
@@ -311,6 +316,12 @@ typedef struct qsamp_counters {
      * not run) */
     int32_t last_stream_rows, last_cluster_rows;
     int32_t last_cluster_size, last_clusters;
+    /* bf16 full-vocabulary rows given to the histogram kernel, how many of
+     * them it handed on to the cluster kernel (read from the last call's
+     * stream-ordered status copy: valid once that call's stream is
+     * synchronised), and its device time */
+    int32_t last_hist_rows, last_hist_handed_on;
+    double last_hist_kernel_ms;
 } qsamp_counters;
 qsamp_status qsamp_get_counters(const qsamp_ctx* ctx, qsamp_counters* out);
 qsamp_status qsamp_set_kernel_timing(qsamp_ctx* ctx, int32_t on);

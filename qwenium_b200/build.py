@@ -11,7 +11,7 @@ ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libqsamp.so")
 SOURCES = [os.path.join(CSRC, f) for f in ("qsamp_kernels.cu", "qsamp_api.cu", "qsamp_static.cu",
                                             "qsamp_trie_api.cpp")] + [os.path.join(HERE, "trie", "compact_trie.cpp")]
-HEADERS = [os.path.join(CSRC, f) for f in ("qs_math.h", "qsamp_device.h")] + [
+HEADERS = [os.path.join(CSRC, f) for f in ("qs_math.h", "qsamp_device.h", "qsamp_hist.cuh")] + [
     os.path.join(ROOT, "include", "qsamp.h"), os.path.join(HERE, "trie", "compact_trie.h")]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # IEEE float semantics are part of the contract: no --use_fast_math.

@@ -399,4 +399,104 @@ QS_HD long long qs_run_add(float* Sp, float t, long long c, float stop) {
     return c;
 }
 
+// qs_run_add_d: qs_run_add for doubles (53-bit significands),
+//     for (i = 0; i < c; ++i) { S = S + t; if (S >= stop) return i; }  return c;
+// with the same per-binade identity: while the exact sum stays in S's binade
+// every add contributes k = rne(t / ulp) ulps (a half-integer t / ulp rounds
+// to the even neighbour), so a run takes O(1) per binade. The draw of
+// std::discrete_distribution accumulates its cumulative weights this way in
+// double (libstdc++'s partial_sum). S >= 0, t >= 0, stop >= 0 (or +inf).
+QS_HD long long qs_run_add_d(double* Sp, double t, long long c, double stop) {
+    double S = *Sp;
+    long long i = 0;
+    const uint64_t M52 = (1ull << 52) - 1ull;
+    const uint64_t tb = qs_d2u(t);
+    const int et = (int)((tb >> 52) & 0x7ffu);
+    const uint64_t mt = et ? ((tb & M52) | (1ull << 52)) : (tb & M52);
+    const int Et = (et ? et : 1) - 1075; /* t = mt * 2^Et */
+    const uint64_t pb = qs_d2u(stop);
+    const int stop_inf = ((pb >> 52) & 0x7ffu) == 0x7ffu;
+    const int ep = (int)((pb >> 52) & 0x7ffu);
+    const uint64_t mp = ep ? ((pb & M52) | (1ull << 52)) : (pb & M52);
+    const int Ep = (ep ? ep : 1) - 1075; /* stop = mp * 2^Ep */
+    const uint64_t lim = 1ull << 53;
+    while (i < c) {
+        const uint64_t sb = qs_d2u(S);
+        const int es = (int)((sb >> 52) & 0x7ffu);
+        if (es == 0 || es >= 2045 || tb == 0u) {
+            S = QS_DADD(S, t);
+            if (S >= stop) { *Sp = S; return i; }
+            ++i;
+            if (tb == 0u) { *Sp = S; return c; }
+            continue;
+        }
+        const uint64_t ms = (sb & M52) | (1ull << 52);
+        const int Es = es - 1075; /* S = ms * 2^Es, ulp = 2^Es */
+        const int d = Es - Et;    /* t / ulp = mt * 2^-d */
+        uint64_t k, n;
+        int tie = 0;
+        if (d <= 0) {
+            if (-d >= 11) { S = QS_DADD(S, t); if (S >= stop) { *Sp = S; return i; } ++i; continue; }
+            n = mt << (-d);
+            k = n;
+        } else if (d >= 64) {
+            n = 0;
+            k = 0; /* t < 2^-11 ulp */
+        } else {
+            n = mt >> d;
+            const uint64_t rem = mt & ((1ull << d) - 1ull), half = 1ull << (d - 1);
+            tie = rem == half;
+            k = n + (rem > half ? 1u : 0u);
+        }
+        if (tie && (ms & 1u)) {
+            const uint64_t r = ms + n + ((ms + n) & 1u);
+            if (r > lim) { S = QS_DADD(S, t); if (S >= stop) { *Sp = S; return i; } ++i; continue; }
+            S = r == lim ? qs_u2d((uint64_t)(es + 1) << 52) : qs_u2d(((uint64_t)es << 52) | (r - (1ull << 52)));
+            if (S >= stop) { *Sp = S; return i; }
+            ++i;
+            continue;
+        }
+        if (tie) k = n + (n & 1u);
+        if (k == 0) {
+            *Sp = S;
+            return (S >= stop) ? i : c;
+        }
+        const uint64_t room = (lim - ms) / k;
+        if (room == 0) {
+            S = QS_DADD(S, t);
+            if (S >= stop) { *Sp = S; return i; }
+            ++i;
+            continue;
+        }
+        const uint64_t left = (uint64_t)(c - i);
+        const uint64_t nadd = room < left ? room : left;
+        if (!stop_inf) {
+            const int D2 = Ep - Es;
+            uint64_t T;
+            int never = 0;
+            if (D2 >= 0) {
+                if (D2 >= 11 || (mp << D2) > (1ull << 62)) never = 1;
+                T = never ? 0 : (mp << D2);
+            } else {
+                const int sh = -D2;
+                T = sh >= 63 ? (mp ? 1u : 0u) : ((mp + (1ull << sh) - 1ull) >> sh);
+            }
+            if (!never) {
+                const uint64_t j = T <= ms ? 1u : (T - ms + k - 1u) / k;
+                if (j <= nadd) {
+                    const uint64_t r = ms + j * k;
+                    S = r == lim ? qs_u2d((uint64_t)(es + 1) << 52) : qs_u2d(((uint64_t)es << 52) | (r - (1ull << 52)));
+                    *Sp = S;
+                    return i + (long long)j - 1;
+                }
+            }
+        }
+        const uint64_t r = ms + nadd * k;
+        S = r == lim ? qs_u2d((uint64_t)(es + 1) << 52) : qs_u2d(((uint64_t)es << 52) | (r - (1ull << 52)));
+        i += (long long)nadd;
+    }
+    *Sp = S;
+    return c;
+}
+
 #endif  // QS_MATH_H

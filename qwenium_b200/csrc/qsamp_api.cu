@@ -32,6 +32,9 @@ extern "C" cudaError_t qs_launch_char_class(const uint16_t* table, int V, int B,
                                             uint32_t* masks, long long mask_stride, int or_into, int num_sms,
                                             cudaStream_t st);
 extern "C" cudaError_t qs_merge_attrs(size_t smem);
+extern "C" size_t qs_hist_smem();
+extern "C" cudaError_t qs_hist_attrs(size_t smem);
+extern "C" cudaError_t qs_launch_hist(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st);
 extern "C" cudaError_t qs_launch_merge(const qs::QsLaunch* a, const float* all_vals, const int32_t* all_ids,
                                        int n_ranks, int kc, int grid, size_t smem, cudaStream_t st);
 
@@ -102,14 +105,18 @@ struct qsamp_ctx {
     int max_rounds = kMaxRounds;
     unsigned long long ready_wait_ns = 1000000000ull;
     int drop_ready_from = -1;
+    // bf16 full-vocabulary rows take the histogram kernel (off: the cluster
+    // kernel serves them; qsamp_set_path)
+    bool use_hist = true;
     size_t attrs_smem = 0;
     size_t max_dyn = 0;    // largest dynamic shared memory a CTA of the kernel may use
     qsamp_counters ctr = {};
     // optional per-kernel device timing: begin / end events of the stream,
     // cluster and merge kernels of the last call
     bool timing = false;
-    cudaEvent_t ev[6] = {};
-    bool ev_used[3] = {false, false, false};
+    cudaEvent_t ev[8] = {};
+    bool ev_used[4] = {false, false, false, false};
+    bool hist_attr = false;
 };
 
 namespace {
@@ -138,7 +145,7 @@ struct Plan {
 // Smallest cluster whose slices fit the per-CTA shared-memory limit; for
 // small batches, wider clusters while every row still gets its own cluster.
 // Kernel slots of the timing events.
-enum { T_STREAM = 0, T_ROWS = 1, T_MERGE = 2 };
+enum { T_STREAM = 0, T_ROWS = 1, T_MERGE = 2, T_HIST = 3 };
 void t_begin(qsamp_ctx* c, int k, cudaStream_t st) {
     if (c->timing) cudaEventRecord(c->ev[2 * k], st);
 }
@@ -304,13 +311,14 @@ qsamp_status read_status(qsamp_ctx* c) {
     int st = 0;
     cudaError_t e = cudaMemcpy(&st, c->status.p, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(c, e, "reading the device status");
-    *c->pinned_status = st;
+    c->pinned_status[0] = st;
     return status_of(c, st);
 }
 
-// Stream-ordered copy of the status word for qsamp_poll_status.
+// Stream-ordered copy of the status words for qsamp_poll_status (and of the
+// count of rows the histogram kernel handed on, for the counters).
 qsamp_status mirror_status(qsamp_ctx* c, cudaStream_t st) {
-    cudaError_t e = cudaMemcpyAsync(c->pinned_status, c->status.p, sizeof(int), cudaMemcpyDeviceToHost, st);
+    cudaError_t e = cudaMemcpyAsync(c->pinned_status, c->status.p, 5 * sizeof(int), cudaMemcpyDeviceToHost, st);
     return e == cudaSuccess ? QSAMP_OK : cuda_fail(c, e, "copying the device status");
 }
 
@@ -334,7 +342,9 @@ qsamp_status qsamp_create(int32_t device, qsamp_ctx** out) {
     cudaSetDevice(device);
     cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
     cudaDeviceGetAttribute(&c->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-    cudaError_t e = c->status.ensure(3);  // [0] status word, [1] cluster row queue, [2] stream row queue
+    // [0] status word, [1] cluster row queue, [2] stream row queue, [3] histogram
+    // row queue, [4] rows the histogram kernel hands to the cluster kernel
+    cudaError_t e = c->status.ensure(8);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
@@ -344,8 +354,8 @@ qsamp_status qsamp_create(int32_t device, qsamp_ctx** out) {
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->copy_done, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaHostAlloc((void**)&c->pinned_one, sizeof(int), cudaHostAllocDefault);
     if (e == cudaSuccess) *c->pinned_one = 1;
-    if (e == cudaSuccess) e = cudaHostAlloc((void**)&c->pinned_status, sizeof(int), cudaHostAllocDefault);
-    if (e == cudaSuccess) *c->pinned_status = 0;
+    if (e == cudaSuccess) e = cudaHostAlloc((void**)&c->pinned_status, 8 * sizeof(int), cudaHostAllocDefault);
+    if (e == cudaSuccess) std::memset(c->pinned_status, 0, 8 * sizeof(int));
     cudaSetDevice(prev);
     if (e != cudaSuccess) {
         qsamp_destroy(c);  // releases whatever was created
@@ -422,7 +432,7 @@ static qsamp_status common_setup(qsamp_ctx* c, const qsamp_batch* b, cudaStream_
     }
     s = ensure_luts(c, b, st);
     if (s != QSAMP_OK) return s;
-    if ((e = cudaMemsetAsync(c->status.p, 0, 3 * sizeof(int), st)) != cudaSuccess) return cuda_fail(c, e, "status reset");
+    if ((e = cudaMemsetAsync(c->status.p, 0, 5 * sizeof(int), st)) != cudaSuccess) return cuda_fail(c, e, "status reset");
 
     a = qs::QsLaunch{};
     a.logits = b->logits;
@@ -474,35 +484,51 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     c->ctr.last_clusters = 0;
 
     // Route rows: greedy rows and top-k rows (k <= 1024) with a penalty
-    // window of at most 1024 ids stream through one CTA each; the rest (full
-    // vocabulary, large k, long windows) use the cluster kernel.
+    // window of at most 1024 ids stream through one CTA each; bf16 rows with
+    // a full-vocabulary top-p (and no forced token, no top list, a window of
+    // at most 1024 ids) take the histogram kernel; the rest (fp32 full
+    // vocabulary, large k, long windows) use the cluster kernel, which also
+    // serves any row the histogram kernel hands on.
     const size_t sn_smem = qs_stream_smem(b->V);
     const bool stream_fits = sn_smem <= c->max_dyn || c->max_dyn == 0;
-    c->h_rows.resize((size_t)B);
-    int n_stream = 0, n_cluster = 0;
+    const size_t hs_smem = qs_hist_smem();
+    const bool hist_fits = b->dtype == QSAMP_BF16 && b->top_cap == 0 && hs_smem <= (size_t)c->smem_optin &&
+                           c->use_hist;
+    auto window_of = [&](int r) -> long long {
+        const qsamp_row_params& p = b->params[r];
+        if (!b->hist) return 0;
+        const bool pen = p.repetition_penalty != 1.0f || p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
+        if (!pen) return 0;
+        const int len = b->hist_len ? b->hist_len[r] : b->hist_stride;
+        const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
+        return (long long)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
+    };
+    auto kind_of = [&](int r) -> int {  // 0 stream, 1 cluster, 2 histogram
+        const qsamp_row_params& p = b->params[r];
+        const long long w = window_of(r);
+        if (stream_fits && (p.temperature <= 0.0f || (p.top_k > 0 && p.top_k < b->V && p.top_k <= qs::KMAX)) &&
+            w <= 1024)
+            return 0;
+        if (hist_fits && p.temperature > 0.0f && !(p.top_k > 0 && p.top_k < b->V) && p.top_p > 0.0f &&
+            p.top_p < 1.0f && p.force_token < 0 && w <= 1024)
+            return 2;
+        return 1;
+    };
+    // the row list: stream rows | cluster rows | slots for rows the histogram
+    // kernel hands on | histogram rows
+    c->h_rows.resize((size_t)2 * B);
+    int n_stream = 0, n_cluster = 0, n_hist = 0;
     for (int r = 0; r < B; ++r) {
-        const qsamp_row_params& p = b->params[r];
-        bool st_ok = stream_fits && (p.temperature <= 0.0f || (p.top_k > 0 && p.top_k < b->V && p.top_k <= qs::KMAX));
-        if (st_ok && b->hist) {
-            const bool pen = p.repetition_penalty != 1.0f || p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
-            const int len = b->hist_len ? b->hist_len[r] : b->hist_stride;
-            const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
-            const long long w = (long long)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
-            if (pen && w > 1024) st_ok = false;
-        }
-        if (st_ok) c->h_rows[(size_t)n_stream++] = r;
+        const int k = kind_of(r);
+        n_stream += k == 0;
+        n_cluster += k == 1;
+        n_hist += k == 2;
     }
-    for (int r = 0, j = n_stream; r < B; ++r) {
-        const qsamp_row_params& p = b->params[r];
-        bool st_ok = stream_fits && (p.temperature <= 0.0f || (p.top_k > 0 && p.top_k < b->V && p.top_k <= qs::KMAX));
-        if (st_ok && b->hist) {
-            const bool pen = p.repetition_penalty != 1.0f || p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
-            const int len = b->hist_len ? b->hist_len[r] : b->hist_stride;
-            const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
-            const long long w = (long long)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
-            if (pen && w > 1024) st_ok = false;
-        }
-        if (!st_ok) c->h_rows[(size_t)j++] = r, ++n_cluster;
+    for (int r = 0, i0 = 0, i1 = n_stream, i2 = n_stream + n_cluster + n_hist; r < B; ++r) {
+        const int k = kind_of(r);
+        if (k == 0) c->h_rows[(size_t)i0++] = r;
+        else if (k == 1) c->h_rows[(size_t)i1++] = r;
+        else c->h_rows[(size_t)i2++] = r;
     }
     // Cluster rows are served from a queue in list order: the ones likely to
     // take longest go first, so that they do not start last and set the
@@ -519,26 +545,42 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         };
         return key(x) > key(y);
     });
-    if ((e = c->rows.ensure(B)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(rows)");
-    if ((e = cudaMemcpyAsync(c->rows.p, c->h_rows.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice, st)) !=
+    const int nlist = n_stream + n_cluster + 2 * n_hist;
+    if ((e = c->rows.ensure(nlist > 0 ? nlist : 1)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(rows)");
+    if ((e = cudaMemcpyAsync(c->rows.p, c->h_rows.data(), sizeof(int32_t) * nlist, cudaMemcpyHostToDevice, st)) !=
         cudaSuccess)
         return cuda_fail(c, e, "copying row lists");
 
-    // With both kinds of rows, the cluster kernel goes first on the caller's
-    // stream and the stream kernel runs beside it on the context's second
-    // stream: clusters of 8 CTAs leave SMs free, which the stream kernel's
-    // CTAs fill. The caller's stream then waits for both (fork / join events).
-    const bool both = n_stream > 0 && n_cluster > 0;
+    // With stream rows and other rows, the others go first on the caller's
+    // stream and the stream kernel runs beside them on the context's second
+    // stream; the caller's stream then waits for both (fork / join events).
+    const bool both = n_stream > 0 && (n_cluster > 0 || n_hist > 0);
     cudaStream_t st2 = both ? c->aux : st;
     if (both) {
         if ((e = cudaEventRecord(c->fork, st)) != cudaSuccess || (e = cudaStreamWaitEvent(st2, c->fork, 0)) != cudaSuccess)
             return cuda_fail(c, e, "fork to the second stream");
     }
-    if (n_cluster > 0) {
+    if (n_hist > 0) {
+        if (!c->hist_attr) {
+            if ((e = qs_hist_attrs(hs_smem)) != cudaSuccess) return cuda_fail(c, e, "histogram kernel attributes");
+            c->hist_attr = true;
+        }
+        qs::QsLaunch ha = a;
+        ha.hs_rows = c->rows.p + n_stream + n_cluster + n_hist;
+        ha.hs_nrows = n_hist;
+        ha.hs_ctr = c->status.p + 3;
+        ha.bail_rows = c->rows.p + n_stream + n_cluster;
+        ha.bail_ctr = c->status.p + 4;
+        const int grid = n_hist < c->num_sms ? n_hist : c->num_sms;
+        t_begin(c, T_HIST, st);
+        if ((e = qs_launch_hist(&ha, grid, hs_smem, st)) != cudaSuccess) return cuda_fail(c, e, "histogram kernel launch");
+        t_end(c, T_HIST, st);
+    }
+    if (n_cluster > 0 || n_hist > 0) {
         Plan plan;
-        s = plan_for(c, n_cluster, b->V, b->dtype == QSAMP_BF16, plan);
+        s = plan_for(c, n_cluster + n_hist, b->V, b->dtype == QSAMP_BF16, plan);
         if (s != QSAMP_OK) return s;
-        if (n_stream > 0) {
+        if (n_stream > 0 && n_cluster > 0) {
             // the SMs split by the rows' expected work (measured on B200, V=151936):
             // a stream row takes about 48 SM-us (half an SM for ~95 us), a
             // cluster row about 140 us on each of its 6 CTAs' SMs, of which
@@ -552,6 +594,7 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         qs::QsLaunch ca = a;
         ca.rows = c->rows.p + n_stream;
         ca.nrows = n_cluster;
+        ca.nrows_dev = n_hist > 0 ? c->status.p + 4 : nullptr;
         ca.n_s = plan.n_s;
         c->ctr.last_cluster_size = plan.cl;
         c->ctr.last_clusters = plan.clusters;
@@ -586,6 +629,7 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     c->ctr.logit_bytes += (uint64_t)B * (uint64_t)b->V * esz;
     c->ctr.last_stream_rows = n_stream;
     c->ctr.last_cluster_rows = n_cluster;
+    c->ctr.last_hist_rows = n_hist;
     return mirror_status(c, st);
 }
 
@@ -738,9 +782,12 @@ qsamp_status qsamp_set_limits(qsamp_ctx* c, const qsamp_limits* l) {
                     (long long)l->ready_wait_ns);
     if (l->drop_ready_from < -1)
         return fail(c, QSAMP_ERR_INVALID_ARG, "limits.drop_ready_from: expected >= -1, got %d", l->drop_ready_from);
+    if (l->hist_path != 0 && l->hist_path != 1)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "limits.hist_path: expected 0 or 1, got %d", l->hist_path);
     c->max_rounds = l->max_rounds;
     c->ready_wait_ns = (unsigned long long)l->ready_wait_ns;
     c->drop_ready_from = l->drop_ready_from;
+    c->use_hist = l->hist_path != 0;
     return QSAMP_OK;
 }
 
@@ -749,18 +796,22 @@ qsamp_status qsamp_get_limits(const qsamp_ctx* c, qsamp_limits* out) {
     out->max_rounds = c->max_rounds;
     out->ready_wait_ns = (int64_t)c->ready_wait_ns;
     out->drop_ready_from = c->drop_ready_from;
+    out->hist_path = c->use_hist ? 1 : 0;
+    out->reserved = 0;
     return QSAMP_OK;
 }
 
 qsamp_status qsamp_get_counters(const qsamp_ctx* c, qsamp_counters* out) {
     if (!c || !out) return QSAMP_ERR_INVALID_ARG;
     *out = c->ctr;
+    out->last_hist_handed_on = c->ctr.last_hist_rows > 0 ? ((volatile int*)c->pinned_status)[4] : 0;
     if (c->timing) {
         int prev = 0;
         cudaGetDevice(&prev);
         if (prev != c->device) cudaSetDevice(c->device);
-        double* dst[3] = {&out->last_stream_kernel_ms, &out->last_rows_kernel_ms, &out->last_merge_kernel_ms};
-        for (int k = 0; k < 3; ++k) {
+        double* dst[4] = {&out->last_stream_kernel_ms, &out->last_rows_kernel_ms, &out->last_merge_kernel_ms,
+                          &out->last_hist_kernel_ms};
+        for (int k = 0; k < 4; ++k) {
             *dst[k] = 0.0;
             float ms = 0.0f;
             if (c->ev_used[k] && cudaEventSynchronize(c->ev[2 * k + 1]) == cudaSuccess &&

@@ -69,6 +69,16 @@ struct QsLaunch {
     const int* ready;
     int ready_rows;
     unsigned long long ready_wait_ns;  // longest wait for one ready flag
+    // the cluster kernel serves rows[0 .. nrows + *nrows_dev) when nrows_dev
+    // is set (rows handed on by the histogram kernel are appended on the device)
+    const int* nrows_dev;
+    // the histogram kernel (bf16 full-vocabulary rows): its rows, its queue,
+    // and where it appends the rows it hands to the cluster kernel
+    const int32_t* hs_rows;
+    int hs_nrows;
+    int* hs_ctr;
+    int32_t* bail_rows;
+    int* bail_ctr;
 };
 
 // Dynamic shared-memory layout; identical on host (sizing) and device.

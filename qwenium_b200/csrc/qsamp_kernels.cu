@@ -834,9 +834,9 @@ __device__ void transform_slice(const RowCtx& r, const QsLaunch& a, const Sm& s,
 // ------------------------------------------------------------ outputs
 // Wait until row `row` of the logits has arrived (a.ready, set by the copy
 // engine after each chunk's copy). Thread 0 polls with an acquire load and
-// backs off; the wait is bounded (about 3 s), after which the status reports
-// DEV_TIMEOUT and the row is processed anyway. Every thread of the CTA must
-// call it (it ends with a block barrier).
+// backs off; the wait is bounded by a.ready_wait_ns, after which the status
+// reports DEV_TIMEOUT and the caller gives the row up (token -1). Every
+// thread of the CTA must call it (it ends with a block barrier).
 // A CTA's fp32 slice comes into shared memory by bulk copies (cp.async.bulk,
 // no multicast) that complete on an mbarrier: one thread issues them, the
 // transform then works in place. The barrier is initialised once per CTA and
@@ -2511,7 +2511,9 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
     if (threadIdx.x == 0) slice_bar_init(&slice_bar);
     __syncthreads();
 
-    const int nrows = a.rows ? a.nrows : a.B;
+    // (rows handed on by the histogram kernel, which ran before this launch
+    // on the same stream, follow the host's rows in the list)
+    const int nrows = a.rows ? a.nrows + (a.nrows_dev ? *a.nrows_dev : 0) : a.B;
     // cluster c starts with row c; later rows come from a queue (a.row_ctr,
     // zero at launch) so that slow rows do not pile up on one cluster
     for (int ri = cid; ri < nrows;) {
@@ -3572,6 +3574,8 @@ __global__ void qs_verify_kernel(const void* logits, int dtype, long long row_st
     out_has[b] = has;
 }
 
+#include "qsamp_hist.cuh"
+
 }  // namespace qs
 
 // launch helpers used by qsamp_api.cu
@@ -3672,6 +3676,14 @@ extern "C" cudaError_t qs_stream_occupancy(size_t smem, int* blocks_per_sm) {
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, qs::qs_stream_kernel, qs::SN_NT, smem);
 }
 
+extern "C" size_t qs_hist_smem() { return (size_t)qs::hs_layout().total; }
+extern "C" cudaError_t qs_hist_attrs(size_t smem) {
+    return cudaFuncSetAttribute(qs::qs_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+extern "C" cudaError_t qs_launch_hist(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st) {
+    qs::qs_hist_kernel<<<grid, qs::HS_NT, smem, st>>>(*a);
+    return cudaGetLastError();
+}
 extern "C" cudaError_t qs_launch_stream(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st) {
     qs::qs_stream_kernel<<<grid, qs::SN_NT, smem, st>>>(*a);
     return cudaGetLastError();

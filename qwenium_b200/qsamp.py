@@ -117,6 +117,9 @@ class _Counters(ctypes.Structure):
         ("last_cluster_rows", ctypes.c_int32),
         ("last_cluster_size", ctypes.c_int32),
         ("last_clusters", ctypes.c_int32),
+        ("last_hist_rows", ctypes.c_int32),
+        ("last_hist_handed_on", ctypes.c_int32),
+        ("last_hist_kernel_ms", ctypes.c_double),
     ]
 
 
@@ -125,6 +128,8 @@ class _Limits(ctypes.Structure):
         ("max_rounds", ctypes.c_int32),
         ("drop_ready_from", ctypes.c_int32),
         ("ready_wait_ns", ctypes.c_int64),
+        ("hist_path", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -345,13 +350,14 @@ class Context:
         self._check(self.lib.qsamp_get_limits(self.h, ctypes.byref(lim)), "qsamp_get_limits")
         return {f: getattr(lim, f) for f, _ in lim._fields_}
 
-    def set_limits(self, max_rounds=None, ready_wait_ns=None, drop_ready_from=None) -> None:
+    def set_limits(self, max_rounds=None, ready_wait_ns=None, drop_ready_from=None, hist_path=None) -> None:
         """qsamp_set_limits; arguments left None keep their current value."""
         cur = self.limits()
         lim = _Limits()
         lim.max_rounds = cur["max_rounds"] if max_rounds is None else int(max_rounds)
         lim.ready_wait_ns = cur["ready_wait_ns"] if ready_wait_ns is None else int(ready_wait_ns)
         lim.drop_ready_from = cur["drop_ready_from"] if drop_ready_from is None else int(drop_ready_from)
+        lim.hist_path = cur["hist_path"] if hist_path is None else int(hist_path)
         self._check(self.lib.qsamp_set_limits(self.h, ctypes.byref(lim)), "qsamp_set_limits")
 
     def verify_greedy(self, logits, row_off, drafts, eos_token: int = -1, stream=None):

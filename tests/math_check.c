@@ -121,6 +121,49 @@ int main(int argc, char** argv) {
             }
         }
 #undef RNG
+    } else if (!strcmp(what, "runaddd")) {
+        /* qs_run_add_d against the sequential double loop: S over binades
+           around 2^-30 .. 2^0 (the cumulative weights of a draw), terms from
+           far below half an ulp up to S, exact ties, counts up to 30000,
+           random or infinite stops (a uniform in [0, 1)) */
+        uint64_t st = 0xC2B2AE3D27D4EB4Full * (part + 1);
+#define RNG() (st ^= st << 13, st ^= st >> 7, st ^= st << 17, st)
+        for (uint64_t cs = 0; cs < nparts; ++cs) {
+            const int e = -(int)(RNG() % 31);
+            uint64_t mant = RNG() & ((1ull << 52) - 1ull);
+            if (RNG() % 4 == 0) mant = ((1ull << 52) - 1ull) - (RNG() % 64);
+            double S0;
+            uint64_t sbits = ((uint64_t)(e + 1023) << 52) | mant;
+            memcpy(&S0, &sbits, 8);
+            if (RNG() % 8 == 0) S0 = 0.0;
+            double t;
+            const int kind = (int)(RNG() % 4);
+            const int es = S0 > 0.0 ? e : -30;
+            if (kind == 0) { /* an exact tie: (n + 1/2) ulp(S0) */
+                t = ((double)(RNG() % 4096) + 0.5) * ldexp(1.0, es - 52);
+            } else if (kind == 1) { /* a tie at half an ulp of a later binade */
+                const double ulp = ldexp(1.0, es - 51 + (int)(RNG() % 3));
+                t = (double)(RNG() % 64) * ulp + 0.5 * ulp;
+            } else {
+                const double f = ldexp((double)(RNG() % 1000000 + 1) / 1e6, -(int)(RNG() % 40));
+                t = (S0 > 0.0 ? S0 : ldexp(1.0, es)) * f * (1.0 + (double)(RNG() % 1000003) * 1e-13);
+            }
+            const long long c = (long long)(RNG() % 30000) + 1;
+            double stop = INFINITY;
+            if (RNG() % 2) stop = (double)(RNG() % ((1ull << 53) - 1)) * ldexp(1.0, -53);
+            double Sa = S0, Sb = S0;
+            long long ia = c;
+            for (long long q = 0; q < c; ++q) {
+                Sa = Sa + t;
+                if (Sa >= stop) { ia = q; break; }
+            }
+            const long long ib = qs_run_add_d(&Sb, t, c, stop);
+            if (ia != ib || memcmp(&Sa, &Sb, 8)) {
+                if (bad < 5) printf("mismatch S0=%a t=%a c=%lld stop=%a: loop (%lld, %a) run (%lld, %a)\n", S0, t, c, stop, ia, Sa, ib, Sb);
+                ++bad;
+            }
+        }
+#undef RNG
     } else if (!strcmp(what, "tanh") || !strcmp(what, "tanhx")) {
         const int list = !strcmp(what, "tanhx");
         const uint64_t lo = 0, hi = 0x7F800000u; /* +0 .. +inf */

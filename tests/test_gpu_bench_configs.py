@@ -68,16 +68,29 @@ def run_device(ctx, cfg):
 
 @pytest.mark.parametrize("B", [256, 1024])
 def test_config4_full_batch(ctx, oracle_mod, B):
+    """Both paths a C4 row can take: the histogram kernel (the default for
+    bf16 full-vocabulary rows) and, with it switched off, the cluster kernel
+    with its 9-CTA plan (which also serves any row the histogram kernel hands
+    on)."""
     cfg = W.config4(4, B=B)
-    got = run_device(ctx, cfg)
-    c = ctx.counters()
-    assert c["last_cluster_rows"] == B and c["last_stream_rows"] == 0
-    assert c["last_cluster_size"] == C4_CLUSTER, c
-    assert c["last_clusters"] < B  # rows come from the queue
     want, _, _, _ = oracle_mod.oracle_sample(cfg["logits"], cfg["params"], cfg["hist"], cfg["hist_len"], None,
                                              cfg["u"], bf16=True)
+    try:
+        ctx.set_limits(hist_path=0)
+        got = run_device(ctx, cfg)
+        c = ctx.counters()
+        assert c["last_cluster_rows"] == B and c["last_stream_rows"] == 0 and c["last_hist_rows"] == 0
+        assert c["last_cluster_size"] == C4_CLUSTER, c
+        assert c["last_clusters"] < B  # rows come from the queue
+        bad = diff_rows(got, want)
+        assert not bad, f"C4 B={B}, cluster kernel: {len(bad)} mismatches, first {bad[:6]}"
+    finally:
+        ctx.set_limits(hist_path=1)
+    got = run_device(ctx, cfg)
+    c = ctx.counters()
+    assert c["last_hist_rows"] == B and c["last_cluster_rows"] == 0, c
     bad = diff_rows(got, want)
-    assert not bad, f"C4 B={B}: {len(bad)} mismatches, first {bad[:6]}"
+    assert not bad, f"C4 B={B}, histogram kernel: {len(bad)} mismatches, first {bad[:6]}"
 
 
 @pytest.fixture(scope="module")

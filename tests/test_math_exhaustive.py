@@ -59,6 +59,17 @@ def test_run_add_matches_sequential_float_loop(checker):
         assert p.returncode == 0 and out.strip().endswith("bad=0"), out
 
 
+def test_run_add_d_matches_sequential_double_loop(checker):
+    """qs_run_add_d (the double form, used for the cumulative weights of the
+    discrete draw over runs of equal probabilities) against `S = S + t; if (S
+    >= stop) break;` in double, including ties and binade crossings."""
+    procs = [subprocess.Popen([checker, "runaddd", str(seed), "20000"], stdout=subprocess.PIPE, text=True)
+             for seed in range(NPARTS)]
+    for p in procs:
+        out, _ = p.communicate()
+        assert p.returncode == 0 and out.strip().endswith("bad=0"), out
+
+
 def test_expf_tab_matches_qs_expf(checker):
     """qs_expf_tab (the kernels' form: shared-memory table, no special-case
     branches) equals qs_expf on every float in [-104, 0] and at -inf."""
