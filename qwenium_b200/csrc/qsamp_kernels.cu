@@ -2464,8 +2464,12 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
             }
             if (w.need >= 0) {
                 bool ovf = false;
+                // the pass that starts the top-p walk re-gathers bin 0 unless
+                // its elements hold one or two values: the walk adds such a
+                // bin in closed form, so its size is no limit
+                const bool first_run = w.stage == ST_CUMWALK && w.cwb == 0 && w.need == 0 && RUNBIN(0);
                 if (m->round >= a.max_rounds) ovf = true;
-                else build_gather_set(s, w.need, ovf);
+                else build_gather_set(s, first_run ? -1 : w.need, ovf);
                 if (ovf) {
                     if (threadIdx.x == 0) {
                         set_status(a.status, DEV_ROUNDS_EXHAUSTED);
