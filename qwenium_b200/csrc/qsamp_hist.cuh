@@ -97,7 +97,7 @@ __device__ __forceinline__ uint32_t hs_count(const uint32_t* hist, int k) {
 
 struct HsMisc {
     float M, S1, S2;
-    int nuniq, bail, changed, top_key, found_id, nwm, next_ri;
+    int nuniq, bail, changed, top_key, found_id, nwm, next_ri, kmin;
 };
 
 // Exclusive scan, in place, of n <= HS_GMAX u64 values; returns the total.
@@ -308,6 +308,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
     int* wm = (int*)(H + HO_WM);
     __shared__ HsMisc hm;
     __shared__ unsigned long long wtot[NWARPS];
+    __shared__ int hs_wc[NWARPS];  // matches per warp (the drawn element's search)
     __shared__ u128 wtot2[NWARPS];
     if (threadIdx.x < 32) exp32[threadIdx.x] = qs_tab_exp32_d[threadIdx.x];
     const float NEG_INF = -__int_as_float(0x7f800000);
@@ -355,6 +356,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             goto next_row;
         }
         {
+            QS_TMARK(row, 0, true);
             // ---- 1. the penalty window: distinct ids with their counts
             for (int q = threadIdx.x; q < HS_HT; q += HS_NT) {
                 hid[q] = -1;
@@ -391,6 +393,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 goto next_row;
             }
             const int nuniq = hm.nuniq;
+            QS_TMARK(row, 1, true);
 
             // ---- 2. the row, once: allow-mask and histogram by key
             int ninf = 0;
@@ -430,6 +433,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 }
             }
             ninf = block_sum_int(ninf, m);  // (its barriers complete the histogram)
+            QS_TMARK(row, 2, true);
 
             // ---- 3. the total (an overflowed bin only lowers it), NaN and
             // infinite patterns, the largest counted key
@@ -517,14 +521,41 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 goto next_row;
             }
             const float M = hm.M;
+            QS_TMARK(row, 3, true);
 
-            // ---- 5. groups: counted keys with x - M >= HS_DMIN, descending
-            // (thread t owns keys [65536 - 128(t+1), 65536 - 128t): thread 0 the
-            // largest), then the window's elements merged in by value
-            const int kbase = 65536 - 128 * (threadIdx.x + 1);
+            // ---- 5. groups: counted keys with x - M >= HS_DMIN, descending.
+            // The key -> value map is monotone, so those keys are the range
+            // [kmin, top key]: kmin by a 32-way search of warp 0, then the
+            // range split evenly, highest keys first, over the threads.
+            if (threadIdx.x < 32) {
+                const int lane = threadIdx.x;
+                auto near = [&](int k) { return __fsub_rn(hs_value(r, (uint32_t)k), M) >= HS_DMIN; };
+                int lo = HS_KLO, hi = HS_KHI;  // the smallest k with near(k) is in [lo, hi] (hi: none)
+                while (hi - lo > 32) {
+                    const int pt = lo + (int)(((long long)(hi - lo) * (lane + 1)) / 32);  // lane 31: hi
+                    const bool t = pt < hi && near(pt);
+                    const uint32_t bt = __ballot_sync(FULLMASK, t) | 0x80000000u;
+                    const int f = __ffs(bt) - 1;  // first point at which near holds (31: hi)
+                    const int pf = lo + (int)(((long long)(hi - lo) * (f + 1)) / 32);
+                    const int pp = f > 0 ? lo + (int)(((long long)(hi - lo) * f) / 32) + 1 : lo;
+                    lo = pp;
+                    hi = pf;
+                }
+                const int kk = lo + lane;
+                const bool t = kk < hi && near(kk);
+                const uint32_t bt = __ballot_sync(FULLMASK, t);
+                if (lane == 0) hm.kmin = bt ? lo + __ffs(bt) - 1 : hi;
+            }
+            __syncthreads();
+            const int kmin = hm.kmin;
+            const int ktop = hm.top_key;
+            const int nkeys = ktop >= kmin ? ktop - kmin + 1 : 0;
+            const int per = (nkeys + HS_NT - 1) / HS_NT;
+            const int khi_t = ktop - per * (int)threadIdx.x;          // this thread: keys (klo_t, khi_t], descending
+            const int klo_t = max(kmin - 1, khi_t - per);
             int mine = 0;
-            for (int k = kbase + 127; k >= kbase; --k)
-                if (hs_count(hist, k) && __fsub_rn(hs_value(r, (uint32_t)k), M) >= HS_DMIN) ++mine;
+            for (int k = khi_t; k > klo_t; --k)
+                if (hs_count(hist, k)) ++mine;
             int npg = 0;
             const int off = block_excl_scan_int(mine, npg, m);
             if (npg + nuniq > HS_GMAX) {
@@ -533,15 +564,12 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             }
             {
                 int at = off;
-                for (int k = kbase + 127; k >= kbase; --k) {
+                for (int k = khi_t; k > klo_t; --k) {
                     const uint32_t c = hs_count(hist, k);
                     if (!c) continue;
-                    const float x = hs_value(r, (uint32_t)k);
-                    if (__fsub_rn(x, M) >= HS_DMIN) {
-                        gx[at] = x;
-                        gc[at] = c;
-                        ++at;
-                    }
+                    gx[at] = hs_value(r, (uint32_t)k);
+                    gc[at] = c;
+                    ++at;
                 }
             }
             __syncthreads();  // (the histogram is read no more)
@@ -562,6 +590,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 __syncthreads();
             }
             const int G = npg + nw;
+            QS_TMARK(row, 4, true);
             // merge: pattern group i goes to i + #{window values > x_i},
             // window element j to j + #{pattern groups with value >= its value}
             {
@@ -644,6 +673,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             }
             __syncthreads();
             const float S1 = hm.S1;
+            QS_TMARK(row, 5, true);
 
             // ---- 6b. the top-p cut: cum += t / sum_exp until cum >= top_p (:173-178)
             for (int g = threadIdx.x; g < G; g += HS_NT) {
@@ -678,6 +708,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             }
             __syncthreads();
             const float S2 = hm.S2;
+            QS_TMARK(row, 6, true);
             // probabilities p = t / sum_keep (:189) over the survivor groups
             const int ng = jc + 1;
             for (int g = threadIdx.x; g < ng; g += HS_NT) gt[g] = __fdiv_rn(gt[g], S2);
@@ -728,6 +759,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 pos = fd < ng ? (long long)pref[fd] + stp[fd] : n_keep - 1;
             }
 
+            QS_TMARK(row, 7, true);
             // ---- 7. the element at sorted position pos: its group, the first
             // group of its value, its rank among the row's elements of that
             // value (ascending id), and the element of that rank
@@ -769,67 +801,114 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 if (wx[u] == xs) wm[atomicAdd(&hm.nwm, 1)] = wid[u];
             __syncthreads();
             const int nwm = hm.nwm;
-            long long acc = 0;
-            const int CH = 8 * HS_NT;
-            for (int c0 = 0; c0 < V; c0 += CH) {
-                const int i0 = c0 + 8 * threadIdx.x;
+            QS_TMARK(row, 10, true);
+            // the 8 elements from i0 (a multiple of 8) that hold value xs:
+            // keys [klo, khi] outside the window and allowed, and the window's
+            // elements of that value; ld8 loads them, flags_of tests them
+            auto ld8 = [&](int i0) -> uint4 {
+                if (i0 >= V) return make_uint4(0u, 0u, 0u, 0u);
+                if (a.vec_ok && i0 + 8 <= V) return __ldg((const uint4*)(rp + i0));
+                uint32_t w[4] = {0u, 0u, 0u, 0u};
+                for (int e = 0; e < 8; ++e)
+                    if (i0 + e < V) w[e >> 1] |= (uint32_t)rp[i0 + e] << ((e & 1) * 16);
+                return make_uint4(w[0], w[1], w[2], w[3]);
+            };
+            auto flags_of = [&](int i0, uint4 q) -> uint32_t {
                 uint32_t flags = 0;
-                if (i0 < V) {
-                    uint32_t b16[8];
-                    if (a.vec_ok && i0 + 8 <= V) {
-                        const uint4 q = __ldg((const uint4*)(rp + i0));
-                        const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+                if (i0 >= V) return 0u;
+                const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) b16[e] = (w4[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) b16[e] = i0 + e < V ? rp[i0 + e] : 0u;
+                for (int e = 0; e < 8; ++e) {
+                    const int i = i0 + e;
+                    const int k = (int)hs_key((w4[e >> 1] >> ((e & 1) * 16)) & 0xffffu);
+                    if (i >= V || k < klo || k > khi) continue;
+                    if (r.mask && !((r.mask[i >> 5] >> (i & 31)) & 1u)) continue;
+                    bool inwin = false;
+                    if (nuniq) {
+                        uint32_t slot = ((uint32_t)i * 2654435761u) & (HS_HT - 1);
+                        while (hid[slot] != -1) {
+                            if (hid[slot] == i) {
+                                inwin = true;
+                                break;
+                            }
+                            slot = (slot + 1) & (HS_HT - 1);
+                        }
                     }
+                    if (!inwin) flags |= 1u << e;
+                }
+                for (int u = 0; u < nwm; ++u) {
+                    const int d = wm[u] - i0;
+                    if (d >= 0 && d < 8) flags |= 1u << d;
+                }
+                return flags;
+            };
+            // the rank-th of them in id order, in super-chunks of 16 x 1024
+            // elements: warp w counts elements [s + 1024 w, s + 1024 (w + 1))
+            // in four 256-element pieces (their loads in flight together); one
+            // prefix over the warps tells whether the rank-th lies in this
+            // super-chunk, and which warp and piece hold it
+            {
+                const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+                long long acc = 0;
+                for (int sc = 0; sc < V; sc += NWARPS * 1024) {
+                    const int wb = sc + warp * 1024;
+                    uint4 qv[4];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int i = i0 + e;
-                        const int k = (int)hs_key(b16[e]);
-                        if (i >= V || k < klo || k > khi) continue;
-                        if (r.mask && !((r.mask[i >> 5] >> (i & 31)) & 1u)) continue;
-                        bool inwin = false;
-                        if (nuniq) {
-                            uint32_t slot = ((uint32_t)i * 2654435761u) & (HS_HT - 1);
-                            while (hid[slot] != -1) {
-                                if (hid[slot] == i) {
-                                    inwin = true;
-                                    break;
-                                }
-                                slot = (slot + 1) & (HS_HT - 1);
+                    for (int u = 0; u < 4; ++u) qv[u] = ld8(wb + u * 256 + 8 * lane);
+                    uint32_t fl[4];
+                    int pc[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        fl[u] = flags_of(wb + u * 256 + 8 * lane, qv[u]);
+                        int cn = __popc(fl[u]);
+                        for (int o = 16; o > 0; o >>= 1) cn += __shfl_xor_sync(FULLMASK, cn, o);
+                        pc[u] = cn;
+                    }
+                    if (lane == 0) hs_wc[warp] = pc[0] + pc[1] + pc[2] + pc[3];
+                    __syncthreads();
+                    long long before = acc;
+                    int tot = 0;
+                    for (int q = 0; q < NWARPS; ++q) {
+                        if (q < warp) before += hs_wc[q];
+                        tot += hs_wc[q];
+                    }
+                    __syncthreads();  // (hs_wc is rewritten by the next super-chunk)
+                    if (acc + tot > rank) {
+                        const int wc = pc[0] + pc[1] + pc[2] + pc[3];
+                        if (rank >= before && rank < before + wc) {
+                            int want = (int)(rank - before);
+                            int u = 0;
+                            while (u < 3 && want >= pc[u]) want -= pc[u++];
+                            uint32_t f = fl[0];
+#pragma unroll
+                            for (int j = 1; j < 4; ++j)
+                                if (u == j) f = fl[j];
+                            const int nm = __popc(f);
+                            int incl = nm;
+                            for (int o = 1; o < 32; o <<= 1) {
+                                const int v = __shfl_up_sync(FULLMASK, incl, o);
+                                if (lane >= o) incl += v;
+                            }
+                            if (want >= incl - nm && want < incl) {
+                                int left = want - (incl - nm);
+                                for (int e = 0; e < 8; ++e)
+                                    if ((f >> e) & 1u) {
+                                        if (left == 0) {
+                                            hm.found_id = wb + u * 256 + 8 * lane + e;
+                                            break;
+                                        }
+                                        --left;
+                                    }
                             }
                         }
-                        if (!inwin) flags |= 1u << e;
+                        break;  // (uniform: every thread saw the same totals)
                     }
-                    for (int u = 0; u < nwm; ++u) {
-                        const int d = wm[u] - i0;
-                        if (d >= 0 && d < 8) flags |= 1u << d;
-                    }
+                    acc += tot;
                 }
-                const int nm = __popc(flags);
-                int tot = 0;
-                const int before = block_excl_scan_int(nm, tot, m);
-                if (acc + tot > rank) {
-                    const long long want = rank - acc;
-                    if (want >= before && want < before + nm) {
-                        int left = (int)(want - before);
-                        for (int e = 0; e < 8; ++e)
-                            if ((flags >> e) & 1u) {
-                                if (left == 0) {
-                                    hm.found_id = i0 + e;
-                                    break;
-                                }
-                                --left;
-                            }
-                    }
-                    break;  // (uniform: every thread saw the same totals)
-                }
-                acc += tot;
             }
             __syncthreads();
+            QS_TMARK(row, 8, true);
+            QS_NOTE(row, 9, G, true);
             if (hm.found_id < 0) {  // (not expected: the groups count these elements)
                 hs_bail(a, row);
                 goto next_row;
