@@ -32,7 +32,9 @@ typedef enum {
     QSAMP_ERR_UNSUPPORTED = 3, /* valid request this build does not serve (message says which) */
     QSAMP_ERR_DEVICE = 4,      /* the kernel reported an internal limit (message says which) */
     QSAMP_ERR_NO_MEMORY = 5,
-    QSAMP_ERR_IO = 6           /* keep-list file unreadable (vocab_utils.h:12-37 throws) */
+    QSAMP_ERR_IO = 6,          /* keep-list file unreadable (vocab_utils.h:12-37 throws) */
+    QSAMP_ERR_TIMEOUT = 7,     /* a collective did not complete by its deadline (qsamp_comm.h) */
+    QSAMP_ERR_COMM = 8         /* a collective failed or its communicator was aborted (qsamp_comm.h) */
 } qsamp_status;
 
 typedef enum { QSAMP_F32 = 0, QSAMP_BF16 = 1 } qsamp_dtype;

@@ -32,6 +32,41 @@ def stale() -> bool:
     return any(os.path.getmtime(p) > t for p in SOURCES + HEADERS)
 
 
+COMM_LIB = os.path.join(HERE, "libqsamp_comm.so")
+COMM_SOURCES = [os.path.join(CSRC, "qsamp_comm.cpp")]
+COMM_HEADERS = [os.path.join(ROOT, "include", "qsamp_comm.h"), os.path.join(ROOT, "include", "qsamp.h")]
+
+
+def nccl_flags() -> list:
+    """Compile and link against the NCCL that torch loads (the nvidia-nccl
+    wheel), so that a process holding both libraries holds one NCCL; the
+    system NCCL otherwise."""
+    try:
+        import nvidia.nccl as nn
+
+        base = os.path.dirname(nn.__file__) if nn.__file__ else list(nn.__path__)[0]
+        inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
+        if os.path.exists(os.path.join(inc, "nccl.h")) and os.path.exists(os.path.join(lib, "libnccl.so.2")):
+            return ["-I" + inc, "-L" + lib, "-Xlinker", "-rpath," + lib, "-l:libnccl.so.2"]
+    except ImportError:
+        pass
+    return ["-lnccl"]
+
+
+def build_comm(force: bool = False) -> str:
+    """libqsamp_comm.so: the NCCL candidate exchange with deadlines (host
+    code; links the system NCCL)."""
+    if not force and os.path.exists(COMM_LIB) and all(
+            os.path.getmtime(p) <= os.path.getmtime(COMM_LIB) for p in COMM_SOURCES + COMM_HEADERS):
+        return COMM_LIB
+    cmd = [nvcc(), "-shared", "-O2", "-std=c++17", "-Xcompiler", "-fPIC", "-Wno-deprecated-gpu-targets", "-o",
+           COMM_LIB, *COMM_SOURCES, *nccl_flags()]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
+    return COMM_LIB
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not stale():
         return LIB
@@ -48,3 +83,4 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
 if __name__ == "__main__":
     print(build(force=True, verbose=True))
+    print(build_comm(force=True))

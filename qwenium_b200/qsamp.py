@@ -57,7 +57,8 @@ ROW_RESULT = np.dtype(
 assert ROW_RESULT.itemsize == 32
 
 QSAMP_F32, QSAMP_BF16 = 0, 1
-STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "UNSUPPORTED", 4: "DEVICE", 5: "NO_MEMORY", 6: "IO"}
+STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "UNSUPPORTED", 4: "DEVICE", 5: "NO_MEMORY", 6: "IO", 7: "TIMEOUT",
+          8: "COMM"}
 
 EXPORTS = (
     "qsamp_create", "qsamp_destroy", "qsamp_last_error", "qsamp_sample", "qsamp_sample_host",
