@@ -163,7 +163,11 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, bool vcounts, Plan& out) {
         cudaError_t e = qs_kernel_static_smem(&st);
         if (e != cudaSuccess) return cuda_fail(c, e, "cudaFuncGetAttributes");
         c->max_dyn = (size_t)c->smem_optin - st;
-        e = qs_kernel_attrs(c->max_dyn);
+    }
+    // (the limit may have been computed by another entry point: the
+    // kernel's own attributes are set here, once per context)
+    if (c->attrs_smem != c->max_dyn) {
+        const cudaError_t e = qs_kernel_attrs(c->max_dyn);
         if (e != cudaSuccess) return cuda_fail(c, e, "cudaFuncSetAttribute");
         c->attrs_smem = c->max_dyn;
     }
@@ -180,7 +184,9 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, bool vcounts, Plan& out) {
     if (first < 0)
         return fail(c, QSAMP_ERR_UNSUPPORTED, "V=%d exceeds the largest vocabulary one 16-CTA cluster holds (%d)", V,
                     16 * (int)((c->max_dyn - (size_t)qs::smem_layout(0, vcounts).total) / 4 / 8 * 8));
-    int pick = first;
+    // (a size the device reports it cannot place -- no cluster of it fits,
+    // whatever the reason -- gives way to the next, smaller slices)
+    int pick = -1;
     for (int i = first; i < 10; ++i) {
         const int cl = sizes[i];
         const int n_s = qs::align_up((V + cl - 1) / cl, 8);
@@ -191,10 +197,15 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, bool vcounts, Plan& out) {
             cudaGetLastError();
             mc = 0;
         }
-        if (mc <= 0) break;
-        if (i == first || mc >= B) pick = i;
+        if (mc <= 0) {
+            if (pick < 0) continue;
+            break;
+        }
+        if (pick < 0 || mc >= B) pick = i;
         if (mc < B) break;
     }
+    if (pick < 0)
+        return fail(c, QSAMP_ERR_UNSUPPORTED, "V=%d: the device can place no thread-block cluster of the kernel", V);
     const int cl = sizes[pick];
     out.cl = cl;
     out.n_s = qs::align_up((V + cl - 1) / cl, 8);

@@ -170,3 +170,28 @@ def test_vshard_rejects_full_vocab_rows(ctx):
         p = W.default_params(4)
         p["top_k"] = 1
         ctx.merge_topk(torch.cat([v] * 3), torch.cat([i] * 3), p)  # 6 x 1024 > 5120 candidates
+
+
+def test_cluster_rows_after_a_sharded_call(oracle_mod):
+    """A context whose first call is qsamp_shard_topk must still serve
+    full-vocabulary rows afterwards (the cluster kernel's launch attributes
+    are set by its own first use, whoever computed the context's limits)."""
+    import torch
+
+    from qwenium_b200 import qsamp
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    c = qsamp.Context(0)
+    cfg = case(71, 8, 50000)
+    c.shard_topk(to_dev(np.ascontiguousarray(cfg["logits"][:, :25000]), False), cfg["params"], 0, 50000, 64,
+                 hist=torch.from_numpy(cfg["hist"]).cuda(), hist_len=cfg["hist_len"])
+    full = case(72, 8, 131072, bf16=True)
+    full["params"]["top_k"] = 0
+    full["params"]["temperature"] = 0.8
+    full["params"]["force_token"] = -1
+    got = run_unsharded(c, full)
+    want, _, _, _ = oracle_mod.oracle_sample(W.f32_to_bf16_bits(full["logits"]), full["params"], full["hist"],
+                                             full["hist_len"], None, full["u"], bf16=True)
+    assert_same(got, want, "full-vocabulary rows after a sharded call")
+    c.close()

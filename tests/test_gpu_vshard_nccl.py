@@ -2,7 +2,9 @@
 
 Each rank holds its contiguous vocabulary slice; qwenium_b200.shard runs
 shard_topk, the NCCL all-gather and merge_topk. Both ranks must return the
-rows the unsharded path returns for the whole vocabulary. Skipped with fewer
+rows the unsharded path returns for the whole vocabulary. A second batch
+mixes in rows with a full-vocabulary top-p (bf16, soft-cap, allow-masks),
+which the shard path transposes with an NCCL all-to-all. Skipped with fewer
 than two GPUs.
 """
 import os
@@ -47,6 +49,23 @@ def _worker(rank, world, port, outdir):
         got = res.cpu().numpy().view(RES).reshape(-1)
         np.save(os.path.join(outdir, f"got{rank}.npy"), got)
         np.save(os.path.join(outdir, f"base{rank}.npy"), base)
+        # rows with a full-vocabulary top-p among candidate rows
+        from test_gpu_vshard import slice_mask
+
+        cfg2 = case(64, 48, 131072, bf16=True, masks=True)
+        p2 = cfg2["params"]
+        p2["top_k"][::3] = 0
+        p2["temperature"][::3] = 0.9
+        V2 = cfg2["logits"].shape[1]
+        base2 = run_unsharded(ctx, cfg2)
+        lo, n = shard.shard_range(V2, world, rank)
+        local2 = to_dev(np.ascontiguousarray(cfg2["logits"][:, lo:lo + n]), True)
+        lmask = torch.from_numpy(np.ascontiguousarray(slice_mask(cfg2["masks"], lo, n)).view(np.int32)).cuda()
+        res2 = shard.sample_vshard(ctx, local2, p2, V2, hist=torch.from_numpy(cfg2["hist"]).cuda(),
+                                   hist_len=cfg2["hist_len"], masks=lmask, u=cfg2["u"])
+        torch.cuda.synchronize()
+        np.save(os.path.join(outdir, f"got2_{rank}.npy"), res2.cpu().numpy().view(RES).reshape(-1))
+        np.save(os.path.join(outdir, f"base2_{rank}.npy"), base2)
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -75,3 +94,5 @@ def test_vshard_two_ranks_nccl(tmp_path):
         got = np.load(tmp_path / f"got{r}.npy")
         base = np.load(tmp_path / f"base{r}.npy")
         assert_same(got, base, f"rank {r}")
+        assert_same(np.load(tmp_path / f"got2_{r}.npy"), np.load(tmp_path / f"base2_{r}.npy"),
+                    f"rank {r}, full-vocabulary rows transposed")

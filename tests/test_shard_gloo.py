@@ -106,3 +106,70 @@ def test_exchange_layout_two_gloo_ranks(tmp_path):
         mv, mi = _topk(vals[keep], ids[keep], k)
         ev, ei = _topk(x[b], np.arange(V, dtype=np.int32), k)
         assert np.array_equal(mi, ei) and np.array_equal(mv, ev)
+
+
+def _transpose_worker(rank, world, port, outdir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        B, V = 7, 2048
+        rng = np.random.default_rng(5)
+        x = rng.standard_normal((B, V)).astype(np.float32)
+        bits = (rng.random((B, V)) < 0.5).astype(np.uint8)
+        words = np.packbits(bits, axis=1, bitorder="little").view(np.int32).reshape(B, V // 32)
+        lo, n = shard.shard_range(V, world, rank)
+        rows = [1, 3, 4, 6]
+        cols = [shard.shard_range(V, world, q)[1] for q in range(world)]
+        own, full = shard.transpose_rows(torch.from_numpy(np.ascontiguousarray(x[:, lo:lo + n])), rows, cols)
+        _, fmask = shard.transpose_rows(torch.from_numpy(np.ascontiguousarray(words[:, lo // 32:(lo + n) // 32])),
+                                        rows, [c // 32 for c in cols])
+        np.save(os.path.join(outdir, f"own{rank}.npy"), own)
+        np.save(os.path.join(outdir, f"full{rank}.npy"), full.numpy())
+        np.save(os.path.join(outdir, f"mask{rank}.npy"), fmask.numpy())
+        # results: row r's record holds r in every byte
+        res = torch.tensor(np.repeat(own.astype(np.uint8)[:, None], 32, axis=1))
+        out = torch.zeros((B, 32), dtype=torch.uint8)
+        shard.gather_results(res, own, B, out)
+        np.save(os.path.join(outdir, f"out{rank}.npy"), out.numpy())
+        np.save(os.path.join(outdir, "x.npy"), x)
+        np.save(os.path.join(outdir, "words.npy"), words)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_full_vocabulary_rows_transpose_two_gloo_ranks(tmp_path):
+    """Rows with a full-vocabulary top-p are moved whole to one rank each
+    (row j of the list to rank j % 2) with their allow-mask words, and the
+    row results come back to every rank."""
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_transpose_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    x, words = np.load(tmp_path / "x.npy"), np.load(tmp_path / "words.npy")
+    rows = [1, 3, 4, 6]
+    for r in range(2):
+        own = np.load(tmp_path / f"own{r}.npy")
+        assert list(own) == rows[r::2]
+        assert np.array_equal(np.load(tmp_path / f"full{r}.npy"), x[own])
+        assert np.array_equal(np.load(tmp_path / f"mask{r}.npy"), words[own])
+        out = np.load(tmp_path / f"out{r}.npy")
+        for b in range(x.shape[0]):
+            assert np.all(out[b] == (b if b in rows else 0)), (r, b, out[b])
