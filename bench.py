@@ -411,6 +411,7 @@ def run_config4(ctx, dev, stream, peak):
                          "bytes_per_launch": alg, "launch_ms": round(hms, 4),
                          "achieved": round(alg / (hms * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(alg / (hms * 1e-3) / 1e9 / peak, 4),
+                         "traffic": ncu_traffic("qs_hist_kernel/config4-B256"),
                          "step_frac": round(256 * per_row / (ms * 1e-3) / 1e9 / peak, 4),
                          "handed_on_rows": [r[8] for r in krec], "cluster_kernel_ms": round(cms, 4),
                          "cluster_plan": {"ctas_per_cluster": krec[0][4], "clusters": krec[0][5]}}}
