@@ -406,6 +406,8 @@ def run_config4(ctx, dev, stream, peak):
     xs.clear()
     hs.clear()
     return {"workload": "config4-B256: bf16 V=262144, soft-cap 30, T 1.0, top-p 0.9, top-k 0, repetition 1.05/512",
+            "softcap_parity": "unpinned: the reference applies the soft-cap as ggml ops (layers/attention.cpp:30-36) "
+                              "and ggml is not in the reference tree; this build uses a correctly rounded tanh",
             "ms_per_step": round(ms, 4), "rows_per_s": round(256 / (ms * 1e-3), 1),
             "roofline": {"bound": "hbm", "kernel": "qs_hist_kernel", "rows_per_launch": hrows,
                          "bytes_per_launch": alg, "launch_ms": round(hms, 4),
