@@ -220,8 +220,9 @@ __device__ __forceinline__ double units_d(u128 u) {
 // the sum; stop_at[g] receives the index of that add inside group g (or
 // cnt[g]). Returns false when the scan did not settle in HS_ITERS passes.
 __device__ bool hs_walk_f(int n, const uint32_t* cnt, const float* term, float* start, unsigned long long* incr,
-                          int* stop_at, float stop, int sh, unsigned long long* wtot, HsMisc* hm) {
+                          int* stop_at, float stop, int sh, unsigned long long* wtot, HsMisc* hm, int* iters = nullptr) {
     for (int it = 0; it < HS_ITERS; ++it) {
+        if (iters) *iters = it + 1;
         for (int g = threadIdx.x; g < n; g += HS_NT) {
             float S = start[g];
             const long long at = qs_run_add(&S, term[g], (long long)cnt[g], stop);
@@ -249,8 +250,9 @@ __device__ bool hs_walk_f(int n, const uint32_t* cnt, const float* term, float* 
 
 // The same in double (units of 2^-96, 128-bit prefix sums), n <= HS_DMAX.
 __device__ bool hs_walk_d(int n, const uint32_t* cnt, const double* term, double* start, u128* incr, int* stop_at,
-                          double stop, u128* wtot, HsMisc* hm) {
+                          double stop, u128* wtot, HsMisc* hm, int* iters = nullptr) {
     for (int it = 0; it < HS_ITERS; ++it) {
+        if (iters) *iters = it + 1;
         for (int g = threadIdx.x; g < n; g += HS_NT) {
             double S = start[g];
             const long long at = qs_run_add_d(&S, term[g], (long long)cnt[g], stop);
@@ -662,7 +664,8 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             hs_scan_u64(inc, G, wtot);
             for (int g = threadIdx.x; g < G; g += HS_NT) sA[g] = g == 0 ? 0.0f : units_f(inc[g], 30);
             __syncthreads();
-            if (!hs_walk_f(G, gc, gt, sA, inc, nullptr, POS_INF, 23, wtot, &hm)) {
+            int it_s = 0, it_c = 0, it_d = 0;
+            if (!hs_walk_f(G, gc, gt, sA, inc, nullptr, POS_INF, 23, wtot, &hm, &it_s)) {
                 hs_bail(a, row);
                 goto next_row;
             }
@@ -684,14 +687,31 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             hs_scan_u64(inc, G, wtot);
             for (int g = threadIdx.x; g < G; g += HS_NT) sB[g] = g == 0 ? 0.0f : units_f(inc[g], 52);
             __syncthreads();
-            if (!hs_walk_f(G, gc, gt, sB, inc, stp, p.top_p, 60, wtot, &hm)) {
-                hs_bail(a, row);
-                goto next_row;
+            // The cut lies before the first group whose exact (real-valued)
+            // start reaches top_p + 1/64 -- the float sum drifts from the exact
+            // one by far less -- and no later group changes the sums before
+            // it: the walk covers those groups, and all of them only if it
+            // finds no cut there.
+            int nwalk = G;
+            {
+                const float thr = __fadd_rn(p.top_p, 0.015625f);
+                for (int g = threadIdx.x; g < G; g += HS_NT)
+                    if (sB[g] >= thr) nwalk = min(nwalk, g);
+                nwalk = max(1, block_min_int(nwalk, m));
             }
             int jc = G;  // the cut group: the first whose sum stopped inside it
-            for (int g = threadIdx.x; g < G; g += HS_NT)
-                if ((uint32_t)stp[g] < gc[g]) jc = min(jc, g);
-            jc = block_min_int(jc, m);
+            while (true) {
+                if (!hs_walk_f(nwalk, gc, gt, sB, inc, stp, p.top_p, 60, wtot, &hm, &it_c)) {
+                    hs_bail(a, row);
+                    goto next_row;
+                }
+                jc = G;
+                for (int g = threadIdx.x; g < nwalk; g += HS_NT)
+                    if ((uint32_t)stp[g] < gc[g]) jc = min(jc, g);
+                jc = block_min_int(jc, m);
+                if (jc < G || nwalk == G) break;
+                nwalk = G;  // (the starts walked so far are exact; the rest keep their guesses)
+            }
             if (jc >= G || jc >= HS_DMAX) {  // a cut below the groups, or too many survivor groups
                 hs_bail(a, row);
                 goto next_row;
@@ -748,7 +768,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 hs_scan_u128(inc2, ng, wtot2);
                 for (int g = threadIdx.x; g < ng; g += HS_NT) sC[g] = g == 0 ? 0.0 : units_d(inc2[g]);
                 __syncthreads();
-                if (!hs_walk_d(ng, gcd, wd, sC, inc2, stp, u, wtot2, &hm)) {
+                if (!hs_walk_d(ng, gcd, wd, sC, inc2, stp, u, wtot2, &hm, &it_d)) {
                     hs_bail(a, row);
                     goto next_row;
                 }
@@ -909,6 +929,10 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             __syncthreads();
             QS_TMARK(row, 8, true);
             QS_NOTE(row, 9, G, true);
+            QS_NOTE(row, 11, it_s, true);
+            QS_NOTE(row, 12, it_c, true);
+            QS_NOTE(row, 13, it_d, true);
+            QS_NOTE(row, 14, jc + 1, true);
             if (hm.found_id < 0) {  // (not expected: the groups count these elements)
                 hs_bail(a, row);
                 goto next_row;
