@@ -140,13 +140,25 @@ qsamp_status qsamp_poll_status(qsamp_ctx* ctx);
  *                   -1 (the default) turns it off.
  *   hist_path       1 (the default): bf16 rows with a full-vocabulary top-p
  *                   take the histogram kernel; 0: the cluster kernel serves
- *                   them (both give the same rows bit for bit). */
+ *                   them (both give the same rows bit for bit).
+ *   live_path       0 (the default): the cluster kernel serves fp32 rows with
+ *                   a full-vocabulary top-p; 1: they are shared between the
+ *                   cluster kernel and the live-list kernel, which serves a
+ *                   row whose elements within 17.5 of its maximum number at
+ *                   most 4096 on one SM (qsamp_sample only; the host entry
+ *                   point keeps them on the cluster kernel). Worth turning on
+ *                   for peaked rows (low temperatures, confident models):
+ *                   measured on B200 with the config2 batches at temperatures
+ *                   0.2-0.6, 9% less time per call; at 0.2-1.2, 1-3% more.
+ *                   2 (tests): the live-list kernel returns every row it
+ *                   takes, and a second cluster launch serves them. All give
+ *                   the same rows bit for bit. */
 typedef struct qsamp_limits {
     int32_t max_rounds;
     int32_t drop_ready_from;
     int64_t ready_wait_ns;
     int32_t hist_path;
-    int32_t reserved;
+    int32_t live_path;
 } qsamp_limits;
 qsamp_status qsamp_set_limits(qsamp_ctx* ctx, const qsamp_limits* limits);
 qsamp_status qsamp_get_limits(const qsamp_ctx* ctx, qsamp_limits* out);
@@ -324,6 +336,12 @@ typedef struct qsamp_counters {
      * synchronised), and its device time */
     int32_t last_hist_rows, last_hist_handed_on;
     double last_hist_kernel_ms;
+    /* fp32 full-vocabulary rows offered to the live-list kernel, how many it
+     * served and how many it returned to the cluster kernel (stream-ordered
+     * copies, valid once the call's stream is synchronised), and its device
+     * time */
+    int32_t last_live_candidates, last_live_rows, last_live_returned, reserved0;
+    double last_live_kernel_ms;
 } qsamp_counters;
 qsamp_status qsamp_get_counters(const qsamp_ctx* ctx, qsamp_counters* out);
 qsamp_status qsamp_set_kernel_timing(qsamp_ctx* ctx, int32_t on);

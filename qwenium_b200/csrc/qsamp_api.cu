@@ -35,6 +35,10 @@ extern "C" cudaError_t qs_merge_attrs(size_t smem);
 extern "C" size_t qs_hist_smem();
 extern "C" cudaError_t qs_hist_attrs(size_t smem);
 extern "C" cudaError_t qs_launch_hist(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st);
+extern "C" size_t qs_live_smem();
+extern "C" int qs_live_vmax();
+extern "C" cudaError_t qs_live_attrs(size_t smem);
+extern "C" cudaError_t qs_launch_live(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st);
 extern "C" cudaError_t qs_launch_merge(const qs::QsLaunch* a, const float* all_vals, const int32_t* all_ids,
                                        int n_ranks, int kc, int grid, size_t smem, cudaStream_t st);
 
@@ -91,6 +95,12 @@ struct qsamp_ctx {
     cudaStream_t stream = nullptr;
     cudaStream_t aux = nullptr;    // second stream of a call: the stream kernel beside the cluster kernel
     cudaEvent_t fork = nullptr, join = nullptr;
+    // third stream: the live-list kernel beside the cluster kernel (fp32
+    // full-vocabulary rows shared through a claim queue, lvq)
+    cudaStream_t aux2 = nullptr;
+    cudaEvent_t fork2 = nullptr, join2 = nullptr;
+    DevBuf<int> lvq;
+    bool live_last = false;        // the last call ran the live-list kernel
     // host entry point: logits copied in row chunks on a copy stream, each
     // chunk followed by a ready flag (a 4-byte copy from pinned memory)
     cudaStream_t copy = nullptr;
@@ -108,14 +118,20 @@ struct qsamp_ctx {
     // bf16 full-vocabulary rows take the histogram kernel (off: the cluster
     // kernel serves them; qsamp_set_path)
     bool use_hist = true;
+    // fp32 full-vocabulary rows shared with the live-list kernel (0, the
+    // default: the cluster kernel serves them alone; 2: tests, every row the
+    // live-list kernel takes is returned and served by the second cluster
+    // launch)
+    int use_live = 0;
+    bool live_attr = false;
     size_t attrs_smem = 0;
     size_t max_dyn = 0;    // largest dynamic shared memory a CTA of the kernel may use
     qsamp_counters ctr = {};
     // optional per-kernel device timing: begin / end events of the stream,
     // cluster and merge kernels of the last call
     bool timing = false;
-    cudaEvent_t ev[8] = {};
-    bool ev_used[4] = {false, false, false, false};
+    cudaEvent_t ev[10] = {};
+    bool ev_used[5] = {false, false, false, false, false};
     bool hist_attr = false;
 };
 
@@ -145,7 +161,7 @@ struct Plan {
 // Smallest cluster whose slices fit the per-CTA shared-memory limit; for
 // small batches, wider clusters while every row still gets its own cluster.
 // Kernel slots of the timing events.
-enum { T_STREAM = 0, T_ROWS = 1, T_MERGE = 2, T_HIST = 3 };
+enum { T_STREAM = 0, T_ROWS = 1, T_MERGE = 2, T_HIST = 3, T_LIVE = 4 };
 void t_begin(qsamp_ctx* c, int k, cudaStream_t st) {
     if (c->timing) cudaEventRecord(c->ev[2 * k], st);
 }
@@ -327,9 +343,12 @@ qsamp_status read_status(qsamp_ctx* c) {
 }
 
 // Stream-ordered copy of the status words for qsamp_poll_status (and of the
-// count of rows the histogram kernel handed on, for the counters).
+// count of rows the histogram kernel handed on, and of the rows the live-list
+// kernel returned and served, for the counters).
 qsamp_status mirror_status(qsamp_ctx* c, cudaStream_t st) {
     cudaError_t e = cudaMemcpyAsync(c->pinned_status, c->status.p, 5 * sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && c->live_last)
+        e = cudaMemcpyAsync(c->pinned_status + 5, c->lvq.p + 2, 2 * sizeof(int), cudaMemcpyDeviceToHost, st);
     return e == cudaSuccess ? QSAMP_OK : cuda_fail(c, e, "copying the device status");
 }
 
@@ -360,6 +379,14 @@ qsamp_status qsamp_create(int32_t device, qsamp_ctx** out) {
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->aux, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming);
+    if (e == cudaSuccess) {
+        // the live-list kernel's stream takes freed SMs before the stream kernel's
+        int lo = 0, hi = 0;
+        e = cudaDeviceGetStreamPriorityRange(&lo, &hi);
+        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&c->aux2, cudaStreamNonBlocking, hi);
+    }
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->fork2, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->join2, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->copy, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->copy_go, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->copy_done, cudaEventDisableTiming);
@@ -395,6 +422,7 @@ void qsamp_destroy(qsamp_ctx* c) {
     c->h_top_probs.release();
     c->h_results.release();
     c->rows.release();
+    c->lvq.release();
     for (cudaEvent_t ev : c->ev)
         if (ev) cudaEventDestroy(ev);
     c->ready.release();
@@ -407,6 +435,9 @@ void qsamp_destroy(qsamp_ctx* c) {
     if (c->fork) cudaEventDestroy(c->fork);
     if (c->join) cudaEventDestroy(c->join);
     if (c->aux) cudaStreamDestroy(c->aux);
+    if (c->fork2) cudaEventDestroy(c->fork2);
+    if (c->join2) cudaEventDestroy(c->join2);
+    if (c->aux2) cudaStreamDestroy(c->aux2);
     if (c->stream) cudaStreamDestroy(c->stream);
     cudaSetDevice(prev);
     delete c;
@@ -497,14 +528,18 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     // Route rows: greedy rows and top-k rows (k <= 1024) with a penalty
     // window of at most 1024 ids stream through one CTA each; bf16 rows with
     // a full-vocabulary top-p (and no forced token, no top list, a window of
-    // at most 1024 ids) take the histogram kernel; the rest (fp32 full
-    // vocabulary, large k, long windows) use the cluster kernel, which also
-    // serves any row the histogram kernel hands on.
+    // at most 1024 ids) take the histogram kernel; fp32 rows of that kind
+    // are shared between the cluster kernel and the live-list kernel; the
+    // rest (large k, long windows, top lists) use the cluster kernel, which
+    // also serves any row the histogram or live-list kernel hands on.
     const size_t sn_smem = qs_stream_smem(b->V);
     const bool stream_fits = sn_smem <= c->max_dyn || c->max_dyn == 0;
     const size_t hs_smem = qs_hist_smem();
     const bool hist_fits = b->dtype == QSAMP_BF16 && b->top_cap == 0 && hs_smem <= (size_t)c->smem_optin &&
                            c->use_hist;
+    const size_t lv_smem = qs_live_smem();
+    const bool live_fits = b->dtype == QSAMP_F32 && b->top_cap == 0 && !ready && c->use_live != 0 &&
+                           lv_smem <= (size_t)c->smem_optin && b->V <= qs_live_vmax();
     auto window_of = [&](int r) -> long long {
         const qsamp_row_params& p = b->params[r];
         if (!b->hist) return 0;
@@ -514,32 +549,36 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
         return (long long)(lb < (unsigned long long)len ? lb : (unsigned long long)len);
     };
-    auto kind_of = [&](int r) -> int {  // 0 stream, 1 cluster, 2 histogram
+    auto kind_of = [&](int r) -> int {  // 0 stream, 1 cluster, 2 histogram, 3 cluster or live-list
         const qsamp_row_params& p = b->params[r];
         const long long w = window_of(r);
         if (stream_fits && (p.temperature <= 0.0f || (p.top_k > 0 && p.top_k < b->V && p.top_k <= qs::KMAX)) &&
             w <= 1024)
             return 0;
-        if (hist_fits && p.temperature > 0.0f && !(p.top_k > 0 && p.top_k < b->V) && p.top_p > 0.0f &&
-            p.top_p < 1.0f && p.force_token < 0 && w <= 1024)
-            return 2;
+        const bool full_top_p = p.temperature > 0.0f && !(p.top_k > 0 && p.top_k < b->V) && p.top_p > 0.0f &&
+                                p.top_p < 1.0f && p.force_token < 0 && w <= 1024;
+        if (hist_fits && full_top_p) return 2;
+        if (live_fits && full_top_p) return 3;
         return 1;
     };
     // the row list: stream rows | cluster rows | slots for rows the histogram
-    // kernel hands on | histogram rows
+    // kernel hands on | histogram rows | rows shared with the live-list kernel
     c->h_rows.resize((size_t)2 * B);
-    int n_stream = 0, n_cluster = 0, n_hist = 0;
+    int n_stream = 0, n_cluster = 0, n_hist = 0, n_live = 0;
     for (int r = 0; r < B; ++r) {
         const int k = kind_of(r);
         n_stream += k == 0;
         n_cluster += k == 1;
         n_hist += k == 2;
+        n_live += k == 3;
     }
-    for (int r = 0, i0 = 0, i1 = n_stream, i2 = n_stream + n_cluster + n_hist; r < B; ++r) {
+    const int off_live = n_stream + n_cluster + 2 * n_hist;
+    for (int r = 0, i0 = 0, i1 = n_stream, i2 = n_stream + n_cluster + n_hist, i3 = off_live; r < B; ++r) {
         const int k = kind_of(r);
         if (k == 0) c->h_rows[(size_t)i0++] = r;
         else if (k == 1) c->h_rows[(size_t)i1++] = r;
-        else c->h_rows[(size_t)i2++] = r;
+        else if (k == 2) c->h_rows[(size_t)i2++] = r;
+        else c->h_rows[(size_t)i3++] = r;
     }
     // Cluster rows are served from a queue in list order: the ones likely to
     // take longest go first, so that they do not start last and set the
@@ -547,7 +586,10 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     // within reach of the maximum: heavier passes and walks), a top-p cutoff
     // adds the cumulative walk; the key is the temperature, plus one for a
     // cutoff. When rows arrive in chunks, rows of earlier chunks go first.
-    std::stable_sort(c->h_rows.begin() + n_stream, c->h_rows.begin() + n_stream + n_cluster, [&](int x, int y) {
+    // The rows shared with the live-list kernel are ordered the same way: the
+    // cluster kernel takes the flattest from the front, the live-list kernel
+    // the most peaked from the back.
+    auto by_weight = [&](int x, int y) {
         if (ready_rows > 0 && x / ready_rows != y / ready_rows) return x / ready_rows < y / ready_rows;
         auto key = [&](int r) {
             const qsamp_row_params& p = b->params[r];
@@ -555,21 +597,48 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
             return T + ((p.top_p > 0.0f && p.top_p < 1.0f) ? 1.0f : 0.0f);
         };
         return key(x) > key(y);
-    });
-    const int nlist = n_stream + n_cluster + 2 * n_hist;
+    };
+    std::stable_sort(c->h_rows.begin() + n_stream, c->h_rows.begin() + n_stream + n_cluster, by_weight);
+    std::stable_sort(c->h_rows.begin() + off_live, c->h_rows.begin() + off_live + n_live, by_weight);
+    const int nlist = off_live + n_live;
     if ((e = c->rows.ensure(nlist > 0 ? nlist : 1)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(rows)");
     if ((e = cudaMemcpyAsync(c->rows.p, c->h_rows.data(), sizeof(int32_t) * nlist, cudaMemcpyHostToDevice, st)) !=
         cudaSuccess)
         return cuda_fail(c, e, "copying row lists");
+    c->live_last = n_live > 0;
+    if (n_live > 0) {
+        // the claim queue: [0] front, [1] back, [2] returned, [3] served, then
+        // the claim words, the return list and the return claims
+        const size_t nq = 4 + 3 * (size_t)n_live;
+        if ((e = c->lvq.ensure(nq)) != cudaSuccess) return cuda_fail(c, e, "cudaMalloc(live-list queue)");
+        if ((e = cudaMemsetAsync(c->lvq.p, 0, nq * sizeof(int), st)) != cudaSuccess)
+            return cuda_fail(c, e, "live-list queue reset");
+        a.lv_rows = c->rows.p + off_live;
+        a.lv_n = n_live;
+        a.lv_q = c->lvq.p;
+        a.lv_taken = c->lvq.p + 4;
+        a.lv_ret = c->lvq.p + 4 + n_live;
+        a.lv_rclaim = c->lvq.p + 4 + 2 * (size_t)n_live;
+        a.lv_serve_returns = c->use_live == 2 ? 0 : 1;
+        a.lv_return_all = c->use_live == 2 ? 1 : 0;
+    }
 
     // With stream rows and other rows, the others go first on the caller's
     // stream and the stream kernel runs beside them on the context's second
     // stream; the caller's stream then waits for both (fork / join events).
-    const bool both = n_stream > 0 && (n_cluster > 0 || n_hist > 0);
+    // The live-list kernel runs on a third stream beside the cluster kernel;
+    // a second cluster launch after both serves the rows it returned that
+    // the first did not take.
+    const bool both = n_stream > 0 && (n_cluster > 0 || n_hist > 0 || n_live > 0);
     cudaStream_t st2 = both ? c->aux : st;
     if (both) {
         if ((e = cudaEventRecord(c->fork, st)) != cudaSuccess || (e = cudaStreamWaitEvent(st2, c->fork, 0)) != cudaSuccess)
             return cuda_fail(c, e, "fork to the second stream");
+    }
+    if (n_live > 0) {
+        if ((e = cudaEventRecord(c->fork2, st)) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(c->aux2, c->fork2, 0)) != cudaSuccess)
+            return cuda_fail(c, e, "fork to the third stream");
     }
     if (n_hist > 0) {
         if (!c->hist_attr) {
@@ -587,20 +656,46 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
         if ((e = qs_launch_hist(&ha, grid, hs_smem, st)) != cudaSuccess) return cuda_fail(c, e, "histogram kernel launch");
         t_end(c, T_HIST, st);
     }
-    if (n_cluster > 0 || n_hist > 0) {
-        Plan plan;
-        s = plan_for(c, n_cluster + n_hist, b->V, b->dtype == QSAMP_BF16, plan);
+    Plan plan;
+    int live_grid = 0;
+    if (n_cluster > 0 || n_hist > 0 || n_live > 0) {
+        s = plan_for(c, n_cluster + n_hist + n_live, b->V, b->dtype == QSAMP_BF16, plan);
         if (s != QSAMP_OK) return s;
-        if (n_stream > 0 && n_cluster > 0) {
+        if (n_live > 0) {
+            // the live-list kernel's CTAs (one SM each), taken from the stream
+            // kernel's share: about 100 SM-us per peaked row, and a flat row
+            // costs it two passes before it returns it; 4 to 16 CTAs (config2
+            // batches, measured on B200: 4 CTAs best; temperatures 0.2-0.6: 16)
+            const double wl = 100.0 * 0.4 * n_live;
+            const double wc = 140.0 * (0.55 * plan.cl + 2.7) * (n_cluster + 0.6 * n_live);
+            const double ws = 48.0 * n_stream;
+            live_grid = (int)std::ceil(c->num_sms * wl / (wl + wc + ws));
+            live_grid = std::max(std::min(4, n_live), std::min(std::min(live_grid, 16), n_live));
+        }
+        if (n_stream > 0 && (n_cluster > 0 || n_live > 0)) {
             // the SMs split by the rows' expected work (measured on B200, V=151936):
             // a stream row takes about 48 SM-us (half an SM for ~95 us), a
             // cluster row about 140 us on each of its 6 CTAs' SMs, of which
             // 0.45 scales with the slice (1 / cl) and 0.55 does not; clusters
-            // leave the stream kernel its share
-            const double ws = 48.0 * n_stream, wc = 140.0 * (0.55 * plan.cl + 2.7) * n_cluster;
+            // leave the stream kernel its share (and the live-list kernel its CTAs)
+            // (the rows shared with the live-list kernel count as cluster rows:
+            // fewer clusters cost more than the live-list kernel saves)
+            const double ws = 48.0 * n_stream, wc = 140.0 * (0.55 * plan.cl + 2.7) * (n_cluster + n_live);
             const int reserve = (int)std::ceil(c->num_sms * ws / (ws + wc));
             const int cap = (c->num_sms - reserve) / plan.cl;
             plan.clusters = std::max(1, std::min(plan.clusters, cap));
+        }
+        if (n_live > 0) {
+            // launched first: its CTAs take their SMs before the stream
+            // kernel's fill the rest (a CTA of it needs a whole SM)
+            if (!c->live_attr) {
+                if ((e = qs_live_attrs(lv_smem)) != cudaSuccess) return cuda_fail(c, e, "live-list kernel attributes");
+                c->live_attr = true;
+            }
+            t_begin(c, T_LIVE, c->aux2);
+            if ((e = qs_launch_live(&a, live_grid, lv_smem, c->aux2)) != cudaSuccess)
+                return cuda_fail(c, e, "live-list kernel launch");
+            t_end(c, T_LIVE, c->aux2);
         }
         qs::QsLaunch ca = a;
         ca.rows = c->rows.p + n_stream;
@@ -631,6 +726,21 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
             return cuda_fail(c, e, "stream kernel launch");
         t_end(c, T_STREAM, st2);
     }
+    if (n_live > 0) {
+        // the rows the live-list kernel returned after the first cluster
+        // launch stopped taking rows (clusters find nothing left and leave)
+        if ((e = cudaEventRecord(c->join2, c->aux2)) != cudaSuccess || (e = cudaStreamWaitEvent(st, c->join2, 0)) != cudaSuccess)
+            return cuda_fail(c, e, "join from the third stream");
+        qs::QsLaunch ca = a;
+        ca.rows = c->rows.p;
+        ca.nrows = 0;
+        ca.nrows_dev = nullptr;
+        ca.n_s = plan.n_s;
+        ca.lv_serve_returns = 1;
+        e = qs_launch_rows(&ca, plan.clusters, plan.cl, plan.smem, st);
+        if (e != cudaSuccess) return cuda_fail(c, e, "selection kernel launch (returned rows)");
+        c->ctr.kernel_launches += 1;
+    }
     if (both) {
         if ((e = cudaEventRecord(c->join, st2)) != cudaSuccess || (e = cudaStreamWaitEvent(st, c->join, 0)) != cudaSuccess)
             return cuda_fail(c, e, "join from the second stream");
@@ -641,6 +751,7 @@ static qsamp_status sample_locked(qsamp_ctx* c, const qsamp_batch* b, cudaStream
     c->ctr.last_stream_rows = n_stream;
     c->ctr.last_cluster_rows = n_cluster;
     c->ctr.last_hist_rows = n_hist;
+    c->ctr.last_live_candidates = n_live;
     return mirror_status(c, st);
 }
 
@@ -795,10 +906,13 @@ qsamp_status qsamp_set_limits(qsamp_ctx* c, const qsamp_limits* l) {
         return fail(c, QSAMP_ERR_INVALID_ARG, "limits.drop_ready_from: expected >= -1, got %d", l->drop_ready_from);
     if (l->hist_path != 0 && l->hist_path != 1)
         return fail(c, QSAMP_ERR_INVALID_ARG, "limits.hist_path: expected 0 or 1, got %d", l->hist_path);
+    if (l->live_path < 0 || l->live_path > 2)
+        return fail(c, QSAMP_ERR_INVALID_ARG, "limits.live_path: expected 0, 1 or 2, got %d", l->live_path);
     c->max_rounds = l->max_rounds;
     c->ready_wait_ns = (unsigned long long)l->ready_wait_ns;
     c->drop_ready_from = l->drop_ready_from;
     c->use_hist = l->hist_path != 0;
+    c->use_live = l->live_path;
     return QSAMP_OK;
 }
 
@@ -808,7 +922,7 @@ qsamp_status qsamp_get_limits(const qsamp_ctx* c, qsamp_limits* out) {
     out->ready_wait_ns = (int64_t)c->ready_wait_ns;
     out->drop_ready_from = c->drop_ready_from;
     out->hist_path = c->use_hist ? 1 : 0;
-    out->reserved = 0;
+    out->live_path = c->use_live;
     return QSAMP_OK;
 }
 
@@ -816,13 +930,15 @@ qsamp_status qsamp_get_counters(const qsamp_ctx* c, qsamp_counters* out) {
     if (!c || !out) return QSAMP_ERR_INVALID_ARG;
     *out = c->ctr;
     out->last_hist_handed_on = c->ctr.last_hist_rows > 0 ? ((volatile int*)c->pinned_status)[4] : 0;
+    out->last_live_returned = c->live_last ? ((volatile int*)c->pinned_status)[5] : 0;
+    out->last_live_rows = c->live_last ? ((volatile int*)c->pinned_status)[6] : 0;
     if (c->timing) {
         int prev = 0;
         cudaGetDevice(&prev);
         if (prev != c->device) cudaSetDevice(c->device);
-        double* dst[4] = {&out->last_stream_kernel_ms, &out->last_rows_kernel_ms, &out->last_merge_kernel_ms,
-                          &out->last_hist_kernel_ms};
-        for (int k = 0; k < 4; ++k) {
+        double* dst[5] = {&out->last_stream_kernel_ms, &out->last_rows_kernel_ms, &out->last_merge_kernel_ms,
+                          &out->last_hist_kernel_ms, &out->last_live_kernel_ms};
+        for (int k = 0; k < 5; ++k) {
             *dst[k] = 0.0;
             float ms = 0.0f;
             if (c->ev_used[k] && cudaEventSynchronize(c->ev[2 * k + 1]) == cudaSuccess &&

@@ -79,6 +79,21 @@ struct QsLaunch {
     int* hs_ctr;
     int32_t* bail_rows;
     int* bail_ctr;
+    // fp32 full-vocabulary rows shared by the cluster kernel and the
+    // live-list kernel (running at the same time): candidates
+    // lv_rows[0, lv_n), highest temperature first. The cluster kernel claims
+    // from the front, the live-list kernel from the back (one claim word per
+    // candidate); rows the live-list kernel returns (entries row + 1, 0 until
+    // written) are served by the cluster kernel and by a second cluster
+    // launch after both.
+    const int32_t* lv_rows;        // null: no candidates
+    int lv_n;
+    int* lv_q;                     // [0] front, [1] back, [2] returned rows, [3] rows the live-list kernel served
+    int* lv_taken;                 // [lv_n]
+    int* lv_ret;                   // [lv_n]
+    int* lv_rclaim;                // [lv_n]
+    int lv_serve_returns;          // cluster kernel: also serve returned rows
+    int lv_return_all;             // live-list kernel (tests): return every row after its passes
 };
 
 // Dynamic shared-memory layout; identical on host (sizing) and device.
@@ -105,6 +120,7 @@ struct __align__(16) Misc {
     int sel_rem;           // broadcast remaining rank
     int sel_cnt;           // broadcast count of the chosen bin
     int next_ri;           // leading CTA: the cluster's next row-list entry
+    int next_row;          //   and the row it names (-1: none left)
     int skip;              // this CTA's row data did not arrive in time (wait ran out)
     int skip_row;          // some CTA of the cluster skips the row: token -1
     unsigned long long sel_remw;  // broadcast remaining weight (weighted select)

@@ -278,6 +278,239 @@ __device__ bool hs_walk_d(int n, const uint32_t* cnt, const double* term, double
     return false;
 }
 
+// The penalty window of a row (sampling.cpp:124-129 with the frequency /
+// presence extension): its distinct ids in wid[0, hm.nuniq), each with its
+// count in an open-addressing table (hid / hcnt, HS_HT slots, cleared here).
+// A window longer than HS_WMAX sets hm.bail. Ends with a barrier.
+__device__ void hs_window(const QsLaunch& a, int row, const qsamp_row_params& p, int V, int32_t* hid, int32_t* hcnt,
+                          int32_t* wid, HsMisc& hm) {
+    for (int q = threadIdx.x; q < HS_HT; q += HS_NT) {
+        hid[q] = -1;
+        hcnt[q] = 0;
+    }
+    __syncthreads();
+    const bool rep_on = p.repetition_penalty != 1.0f;
+    const bool fp_on = p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f;
+    if ((rep_on || fp_on) && a.hist) {
+        const int len = a.hist_len ? a.hist_len[row] : a.hist_stride;
+        const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
+        const int wl = len > 0 ? (int)(lb < (unsigned long long)len ? lb : (unsigned long long)len) : 0;
+        if (wl > HS_WMAX) {
+            if (threadIdx.x == 0) hm.bail = 1;
+        } else {
+            const int32_t* h = a.hist + (size_t)row * (size_t)a.hist_stride + (len - wl);
+            for (int j = threadIdx.x; j < wl; j += HS_NT) {
+                const int32_t id = h[j];
+                if (id < 0 || id >= V) continue;
+                uint32_t slot = ((uint32_t)id * 2654435761u) & (HS_HT - 1);
+                while (true) {  // at most HS_WMAX <= HS_HT / 2 distinct ids: a free slot exists
+                    const int old = atomicCAS(&hid[slot], -1, id);
+                    if (old == -1 || old == id) {
+                        if (atomicAdd(&hcnt[slot], 1) == 0) wid[atomicAdd(&hm.nuniq, 1)] = id;
+                        break;
+                    }
+                    slot = (slot + 1) & (HS_HT - 1);
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+// The count of window id `id` (present in the table).
+__device__ __forceinline__ int hs_window_count(const int32_t* hid, const int32_t* hcnt, int id) {
+    uint32_t slot = ((uint32_t)id * 2654435761u) & (HS_HT - 1);
+    while (hid[slot] != id) slot = (slot + 1) & (HS_HT - 1);
+    return hcnt[slot];
+}
+// The penalised value of window element v (after the soft-cap and the
+// allow-mask: -inf when masked), then /T and canon (sampling.cpp:130-135,
+// 154-156).
+__device__ __forceinline__ float hs_penalise(const RowCtx& r, const qsamp_row_params& p, float v, int c) {
+    if (p.repetition_penalty != 1.0f)
+        v = v < 0.0f ? __fmul_rn(v, p.repetition_penalty) : __fdiv_rn(v, p.repetition_penalty);
+    if (p.frequency_penalty != 0.0f || p.presence_penalty != 0.0f) {
+        v = __fsub_rn(v, __fmul_rn((float)c, p.frequency_penalty));
+        v = __fsub_rn(v, p.presence_penalty);
+    }
+    return post_value(r, v);
+}
+
+// The scratch arrays of the sums and the draw (inside the histogram's 128 KB
+// in both kernels that use them).
+struct HsArrays {
+    float* sA;
+    unsigned long long* inc;
+    float* sB;
+    int* stp;
+    unsigned long long* pref;  // group start positions (set by the caller)
+    u128* inc2;
+    double* wd;
+    double* sC;
+    uint32_t* gcd;
+};
+__device__ __forceinline__ HsArrays hs_arrays(unsigned char* H) {
+    HsArrays w;
+    w.sA = (float*)(H + HO_SA);
+    w.inc = (unsigned long long*)(H + HO_INC);
+    w.sB = (float*)(H + HO_SB);
+    w.stp = (int*)(H + HO_STP);
+    w.pref = (unsigned long long*)(H + HO_PREF);
+    w.inc2 = (u128*)(H + HO_INC2);
+    w.wd = (double*)(H + HO_WD);
+    w.sC = (double*)(H + HO_SC);
+    w.gcd = (uint32_t*)(H + HO_GCD);
+    return w;
+}
+// What the sums and the draw give: the row's sums, the kept count, the drawn
+// sorted position, its group and probability.
+struct HsDrawn {
+    float S1, S2, prob;
+    long long n_keep, pos;
+    int gp, jc, it_s, it_c, it_d;
+};
+
+// The reference's sums and draw over the row's groups (gx: values in
+// descending order, gc: counts, w.pref: start positions, G <= HS_GMAX groups
+// that hold every element within HS_DMIN of the maximum M). gt is scratch.
+// Returns false when the row cannot be proven exact here (a scan that does
+// not settle, a cut below the groups, too many survivor groups, a normaliser
+// that is not exact in double); the caller hands it on.
+__device__ bool hs_sums_draw(const QsLaunch& a, int row, const qsamp_row_params& p, int G, const float* gx,
+                             const uint32_t* gc, float* gt, const HsArrays& w, const uint64_t* exp32, float M,
+                             HsMisc& hm, unsigned long long* wtot, u128* wtot2, Misc* m, HsDrawn& o) {
+    const float POS_INF = __int_as_float(0x7f800000);
+    float* const sA = w.sA;
+    unsigned long long* const inc = w.inc;
+    float* const sB = w.sB;
+    int* const stp = w.stp;
+    const unsigned long long* const pref = w.pref;
+    // ---- sum_exp: t = expf(x - M) in sorted order (sampling.cpp:171)
+    for (int g = threadIdx.x; g < G; g += HS_NT) gt[g] = qs_expf_tab(__fsub_rn(gx[g], M), exp32);
+    __syncthreads();
+    // starts guessed from the exact masses (a prefix of count * t)
+    for (int g = threadIdx.x; g < G; g += HS_NT) inc[g] = (unsigned long long)gc[g] * f_units(gt[g], 30);
+    __syncthreads();
+    hs_scan_u64(inc, G, wtot);
+    for (int g = threadIdx.x; g < G; g += HS_NT) sA[g] = g == 0 ? 0.0f : units_f(inc[g], 30);
+    __syncthreads();
+    o.it_s = o.it_c = o.it_d = 0;
+    if (!hs_walk_f(G, gc, gt, sA, inc, nullptr, POS_INF, 23, wtot, &hm, &o.it_s)) return false;
+    if (threadIdx.x == 0) {
+        float S = sA[G - 1];
+        qs_run_add(&S, gt[G - 1], (long long)gc[G - 1], POS_INF);
+        hm.S1 = S;
+    }
+    __syncthreads();
+    const float S1 = hm.S1;
+    QS_TMARK(row, 5, true);
+
+    // ---- the top-p cut: cum += t / sum_exp until cum >= top_p (:173-178)
+    for (int g = threadIdx.x; g < G; g += HS_NT) {
+        gt[g] = __fdiv_rn(gt[g], S1);
+        inc[g] = (unsigned long long)gc[g] * f_units(gt[g], 52);
+    }
+    __syncthreads();
+    hs_scan_u64(inc, G, wtot);
+    for (int g = threadIdx.x; g < G; g += HS_NT) sB[g] = g == 0 ? 0.0f : units_f(inc[g], 52);
+    __syncthreads();
+    // The cut lies before the first group whose exact (real-valued) start
+    // reaches top_p + 1/64 -- the float sum drifts from the exact one by far
+    // less -- and no later group changes the sums before it: the walk covers
+    // those groups, and all of them only if it finds no cut there.
+    int nwalk = G;
+    {
+        const float thr = __fadd_rn(p.top_p, 0.015625f);
+        for (int g = threadIdx.x; g < G; g += HS_NT)
+            if (sB[g] >= thr) nwalk = min(nwalk, g);
+        nwalk = max(1, block_min_int(nwalk, m));
+    }
+    int jc = G;  // the cut group: the first whose sum stopped inside it
+    while (true) {
+        if (!hs_walk_f(nwalk, gc, gt, sB, inc, stp, p.top_p, 60, wtot, &hm, &o.it_c)) return false;
+        jc = G;
+        for (int g = threadIdx.x; g < nwalk; g += HS_NT)
+            if ((uint32_t)stp[g] < gc[g]) jc = min(jc, g);
+        jc = block_min_int(jc, m);
+        if (jc < G || nwalk == G) break;
+        nwalk = G;  // (the starts walked so far are exact; the rest keep their guesses)
+    }
+    if (jc >= G || jc >= HS_DMAX) return false;  // a cut below the groups, or too many survivor groups
+    const int sc = stp[jc];  // index of the cutting add inside group jc
+    const long long n_keep = (long long)pref[jc] + sc + 1;
+    // sum_keep: the first n_keep terms of the sum_exp order (:184-188)
+    for (int g = threadIdx.x; g <= jc; g += HS_NT) gt[g] = qs_expf_tab(__fsub_rn(gx[g], M), exp32);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float S = sA[jc];
+        qs_run_add(&S, gt[jc], (long long)sc + 1, POS_INF);
+        hm.S2 = S;
+    }
+    __syncthreads();
+    const float S2 = hm.S2;
+    QS_TMARK(row, 6, true);
+    // probabilities p = t / sum_keep (:189) over the survivor groups
+    const int ng = jc + 1;
+    for (int g = threadIdx.x; g < ng; g += HS_NT) gt[g] = __fdiv_rn(gt[g], S2);
+    __syncthreads();
+
+    // ---- the draw (std::discrete_distribution, :192-193)
+    long long pos = 0;
+    if (n_keep >= 2) {
+        // the normaliser, the probabilities summed in double: exact (every
+        // partial sum a multiple of 2^-52 below 2) when the smallest
+        // probability is at least 2^-29
+        if (!(gt[jc] >= 0x1p-29f)) return false;
+        u128* const inc2 = w.inc2;
+        double* const wd = w.wd;
+        double* const sC = w.sC;
+        uint32_t* const gcd = w.gcd;
+        for (int g = threadIdx.x; g < ng; g += HS_NT) {
+            const unsigned long long cg = g == jc ? (unsigned long long)(sc + 1) : gc[g];
+            inc[g] = cg * f_units(gt[g], 52);
+        }
+        __syncthreads();
+        const unsigned long long Dn = hs_scan_u64(inc, ng, wtot);
+        if (Dn >= (1ull << 53)) return false;
+        const double D = (double)Dn * 0x1p-52;
+        const double u = row_u(a, row, p);
+        // cumulative weights w = p / D over the first n_keep - 1 survivors
+        // (the last survivor's is 1.0)
+        for (int g = threadIdx.x; g < ng; g += HS_NT) {
+            wd[g] = __ddiv_rn((double)gt[g], D);
+            gcd[g] = g == jc ? (uint32_t)sc : gc[g];
+        }
+        __syncthreads();
+        for (int g = threadIdx.x; g < ng; g += HS_NT) inc2[g] = (u128)gcd[g] * d_units(wd[g]);
+        __syncthreads();
+        hs_scan_u128(inc2, ng, wtot2);
+        for (int g = threadIdx.x; g < ng; g += HS_NT) sC[g] = g == 0 ? 0.0 : units_d(inc2[g]);
+        __syncthreads();
+        if (!hs_walk_d(ng, gcd, wd, sC, inc2, stp, u, wtot2, &hm, &o.it_d)) return false;
+        int fd = G;
+        for (int g = threadIdx.x; g < ng; g += HS_NT)
+            if ((uint32_t)stp[g] < gcd[g]) fd = min(fd, g);
+        fd = block_min_int(fd, m);
+        pos = fd < ng ? (long long)pref[fd] + stp[fd] : n_keep - 1;
+    }
+    QS_TMARK(row, 7, true);
+    // the group holding sorted position pos: the last group starting at or
+    // before it
+    int lo = 0, hi = G;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if ((long long)pref[mid] <= pos) lo = mid;
+        else hi = mid;
+    }
+    o.S1 = S1;
+    o.S2 = S2;
+    o.n_keep = n_keep;
+    o.pos = pos;
+    o.gp = lo;
+    o.jc = jc;
+    o.prob = gt[lo];
+    return true;
+}
+
 // Hands the row to the cluster kernel (thread 0; the caller then leaves the row).
 __device__ __forceinline__ void hs_bail(const QsLaunch& a, int row) {
     if (threadIdx.x == 0) a.bail_rows[atomicAdd(a.bail_ctr, 1)] = row;
@@ -360,36 +593,8 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
         {
             QS_TMARK(row, 0, true);
             // ---- 1. the penalty window: distinct ids with their counts
-            for (int q = threadIdx.x; q < HS_HT; q += HS_NT) {
-                hid[q] = -1;
-                hcnt[q] = 0;
-            }
             for (int q = threadIdx.x; q < 65536 / 8; q += HS_NT) ((uint4*)hist)[q] = make_uint4(0u, 0u, 0u, 0u);
-            __syncthreads();
-            if ((rep_on || fp_on) && a.hist) {
-                const int len = a.hist_len ? a.hist_len[row] : a.hist_stride;
-                const unsigned long long lb = (unsigned long long)(long long)p.repetition_lookback;
-                const int wl = len > 0 ? (int)(lb < (unsigned long long)len ? lb : (unsigned long long)len) : 0;
-                if (wl > HS_WMAX) {
-                    if (threadIdx.x == 0) hm.bail = 1;
-                } else {
-                    const int32_t* h = a.hist + (size_t)row * (size_t)a.hist_stride + (len - wl);
-                    for (int j = threadIdx.x; j < wl; j += HS_NT) {
-                        const int32_t id = h[j];
-                        if (id < 0 || id >= V) continue;
-                        uint32_t slot = ((uint32_t)id * 2654435761u) & (HS_HT - 1);
-                        while (true) {  // at most HS_WMAX <= HS_HT / 2 distinct ids: a free slot exists
-                            const int old = atomicCAS(&hid[slot], -1, id);
-                            if (old == -1 || old == id) {
-                                if (atomicAdd(&hcnt[slot], 1) == 0) wid[atomicAdd(&hm.nuniq, 1)] = id;
-                                break;
-                            }
-                            slot = (slot + 1) & (HS_HT - 1);
-                        }
-                    }
-                }
-            }
-            __syncthreads();
+            hs_window(a, row, p, V, hid, hcnt, wid, hm);
             if (hm.bail) {
                 hs_bail(a, row);
                 goto next_row;
@@ -655,149 +860,22 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             __syncthreads();
             hs_scan_u64(pref, G, wtot);
 
-            // ---- 6a. sum_exp: t = expf(x - M) in sorted order (sampling.cpp:171)
-            for (int g = threadIdx.x; g < G; g += HS_NT) gt[g] = qs_expf_tab(__fsub_rn(gx[g], M), exp32);
-            __syncthreads();
-            // starts guessed from the exact masses (a prefix of count * t)
-            for (int g = threadIdx.x; g < G; g += HS_NT) inc[g] = (unsigned long long)gc[g] * f_units(gt[g], 30);
-            __syncthreads();
-            hs_scan_u64(inc, G, wtot);
-            for (int g = threadIdx.x; g < G; g += HS_NT) sA[g] = g == 0 ? 0.0f : units_f(inc[g], 30);
-            __syncthreads();
-            int it_s = 0, it_c = 0, it_d = 0;
-            if (!hs_walk_f(G, gc, gt, sA, inc, nullptr, POS_INF, 23, wtot, &hm, &it_s)) {
+            // ---- 6. the sums and the draw over the groups
+            HsDrawn dr;
+            if (!hs_sums_draw(a, row, p, G, gx, gc, gt, hs_arrays(H), exp32, M, hm, wtot, wtot2, m, dr)) {
                 hs_bail(a, row);
                 goto next_row;
             }
-            if (threadIdx.x == 0) {
-                float S = sA[G - 1];
-                qs_run_add(&S, gt[G - 1], (long long)gc[G - 1], POS_INF);
-                hm.S1 = S;
-            }
-            __syncthreads();
-            const float S1 = hm.S1;
-            QS_TMARK(row, 5, true);
-
-            // ---- 6b. the top-p cut: cum += t / sum_exp until cum >= top_p (:173-178)
-            for (int g = threadIdx.x; g < G; g += HS_NT) {
-                gt[g] = __fdiv_rn(gt[g], S1);
-                inc[g] = (unsigned long long)gc[g] * f_units(gt[g], 52);
-            }
-            __syncthreads();
-            hs_scan_u64(inc, G, wtot);
-            for (int g = threadIdx.x; g < G; g += HS_NT) sB[g] = g == 0 ? 0.0f : units_f(inc[g], 52);
-            __syncthreads();
-            // The cut lies before the first group whose exact (real-valued)
-            // start reaches top_p + 1/64 -- the float sum drifts from the exact
-            // one by far less -- and no later group changes the sums before
-            // it: the walk covers those groups, and all of them only if it
-            // finds no cut there.
-            int nwalk = G;
-            {
-                const float thr = __fadd_rn(p.top_p, 0.015625f);
-                for (int g = threadIdx.x; g < G; g += HS_NT)
-                    if (sB[g] >= thr) nwalk = min(nwalk, g);
-                nwalk = max(1, block_min_int(nwalk, m));
-            }
-            int jc = G;  // the cut group: the first whose sum stopped inside it
-            while (true) {
-                if (!hs_walk_f(nwalk, gc, gt, sB, inc, stp, p.top_p, 60, wtot, &hm, &it_c)) {
-                    hs_bail(a, row);
-                    goto next_row;
-                }
-                jc = G;
-                for (int g = threadIdx.x; g < nwalk; g += HS_NT)
-                    if ((uint32_t)stp[g] < gc[g]) jc = min(jc, g);
-                jc = block_min_int(jc, m);
-                if (jc < G || nwalk == G) break;
-                nwalk = G;  // (the starts walked so far are exact; the rest keep their guesses)
-            }
-            if (jc >= G || jc >= HS_DMAX) {  // a cut below the groups, or too many survivor groups
-                hs_bail(a, row);
-                goto next_row;
-            }
-            const int sc = stp[jc];  // index of the cutting add inside group jc
-            const long long n_keep = (long long)pref[jc] + sc + 1;
-            // sum_keep: the first n_keep terms of the sum_exp order (:184-188)
-            for (int g = threadIdx.x; g <= jc; g += HS_NT) gt[g] = qs_expf_tab(__fsub_rn(gx[g], M), exp32);
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                float S = sA[jc];
-                qs_run_add(&S, gt[jc], (long long)sc + 1, POS_INF);
-                hm.S2 = S;
-            }
-            __syncthreads();
-            const float S2 = hm.S2;
-            QS_TMARK(row, 6, true);
-            // probabilities p = t / sum_keep (:189) over the survivor groups
-            const int ng = jc + 1;
-            for (int g = threadIdx.x; g < ng; g += HS_NT) gt[g] = __fdiv_rn(gt[g], S2);
-            __syncthreads();
-
-            // ---- 6c. the draw (std::discrete_distribution, :192-193)
-            long long pos = 0;
-            if (n_keep >= 2) {
-                // the normaliser, the probabilities summed in double: exact
-                // (every partial sum a multiple of 2^-52 below 2) when the
-                // smallest probability is at least 2^-29
-                if (!(gt[jc] >= 0x1p-29f)) {
-                    hs_bail(a, row);
-                    goto next_row;
-                }
-                for (int g = threadIdx.x; g < ng; g += HS_NT) {
-                    const unsigned long long cg = g == jc ? (unsigned long long)(sc + 1) : gc[g];
-                    inc[g] = cg * f_units(gt[g], 52);
-                }
-                __syncthreads();
-                const unsigned long long Dn = hs_scan_u64(inc, ng, wtot);
-                if (Dn >= (1ull << 53)) {
-                    hs_bail(a, row);
-                    goto next_row;
-                }
-                const double D = (double)Dn * 0x1p-52;
-                const double u = row_u(a, row, p);
-                // cumulative weights w = p / D over the first n_keep - 1
-                // survivors (the last survivor's is 1.0)
-                for (int g = threadIdx.x; g < ng; g += HS_NT) {
-                    wd[g] = __ddiv_rn((double)gt[g], D);
-                    gcd[g] = g == jc ? (uint32_t)sc : gc[g];
-                }
-                __syncthreads();
-                for (int g = threadIdx.x; g < ng; g += HS_NT) inc2[g] = (u128)gcd[g] * d_units(wd[g]);
-                __syncthreads();
-                hs_scan_u128(inc2, ng, wtot2);
-                for (int g = threadIdx.x; g < ng; g += HS_NT) sC[g] = g == 0 ? 0.0 : units_d(inc2[g]);
-                __syncthreads();
-                if (!hs_walk_d(ng, gcd, wd, sC, inc2, stp, u, wtot2, &hm, &it_d)) {
-                    hs_bail(a, row);
-                    goto next_row;
-                }
-                int fd = G;
-                for (int g = threadIdx.x; g < ng; g += HS_NT)
-                    if ((uint32_t)stp[g] < gcd[g]) fd = min(fd, g);
-                fd = block_min_int(fd, m);
-                pos = fd < ng ? (long long)pref[fd] + stp[fd] : n_keep - 1;
-            }
-
-            QS_TMARK(row, 7, true);
-            // ---- 7. the element at sorted position pos: its group, the first
-            // group of its value, its rank among the row's elements of that
-            // value (ascending id), and the element of that rank
-            int gp = 0;
-            {
-                int lo = 0, hi = G;  // the last group starting at or before pos
-                while (hi - lo > 1) {
-                    const int mid = (lo + hi) >> 1;
-                    if ((long long)pref[mid] <= pos) lo = mid;
-                    else hi = mid;
-                }
-                gp = lo;
-            }
+            const float S1 = dr.S1, S2 = dr.S2, prob = dr.prob;
+            const long long n_keep = dr.n_keep, pos = dr.pos;
+            const int gp = dr.gp, jc = dr.jc, it_s = dr.it_s, it_c = dr.it_c, it_d = dr.it_d;
+            // ---- 7. the element at sorted position pos: the first group of
+            // its value, its rank among the row's elements of that value
+            // (ascending id), and the element of that rank
             const float xs = gx[gp];
             int glo = gp;
             while (glo > 0 && gx[glo - 1] == xs) --glo;
             const long long rank = pos - (long long)pref[glo];
-            const float prob = gt[gp];
             // the keys whose (non-window) elements have value xs: [klo, khi]
             int klo, khi;
             {

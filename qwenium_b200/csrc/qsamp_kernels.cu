@@ -496,13 +496,18 @@ __device__ __forceinline__ int next_pow2(int n) {
 // ------------------------------------------------------------ exact walks
 // One full warp emulates `for (i < n) { S = S + term(i); if (S >= stop) return i; }`
 // (float, round to nearest) for non-negative, non-increasing terms with
-// S >= every term already added. Returns the stopping index or n.
-template <typename TermF>
-__device__ int warp_walk_terms(float& S, int n, float stop, TermF term) {
+// S >= every term already added. Returns the stopping index or n. at(i, S)
+// is called by one lane for every term added, with the sum before it.
+struct NoAt {
+    __device__ void operator()(int, float) const {}
+};
+template <typename TermF, typename AtF = NoAt>
+__device__ int warp_walk_terms(float& S, int n, float stop, TermF term, AtF at = AtF()) {
     const int lane = threadIdx.x & 31;
     int i = 0;
     while (i < n) {
         if (!(S > 0.0f)) {
+            if (lane == 0) at(i, S);
             S = __fadd_rn(S, term(i));
             if (S >= stop) return i;
             ++i;
@@ -529,6 +534,8 @@ __device__ int warp_walk_terms(float& S, int n, float stop, TermF term) {
         const int L = (okm == FULLMASK) ? 32 : (__ffs(~okm) - 1);
         const uint32_t below = L == 32 ? FULLMASK : ((1u << L) - 1u);
         const uint32_t hitm = __ballot_sync(FULLMASK, ok && after >= stop) & below;
+        const int Lt = hitm ? __ffs(hitm) : L;  // terms added in this step
+        if (lane < Lt) at(idx, __fmul_rn((float)(m + prev), down));
         if (hitm) {
             const int Ls = __ffs(hitm) - 1;
             S = __shfl_sync(FULLMASK, after, Ls);
@@ -539,6 +546,7 @@ __device__ int warp_walk_terms(float& S, int n, float stop, TermF term) {
             i += L;
         }
         if (L < 32 && i < n) {
+            if (lane == 0) at(i, S);
             S = __fadd_rn(S, term(i));
             if (S >= stop) return i;
             ++i;
@@ -559,16 +567,7 @@ __device__ __forceinline__ int s_dead_bin(float S) {
     return d > NB - 1 ? NB - 1 : (int)d;
 }
 
-// The whole CTA advances S over bins [b, bend) whose k-sums (at binade g[b])
-// are valid for the current S; stops at the first bin that needs its
-// elements (returned), or at bend. Optionally records S at each bin start.
-// The k-sums are read as the exclusive prefix E = s.ksum over the last pass's
-// bin range (prefix_ksums): within one binade of S the sum after bin b is
-// n = m + E[b+1] - E[b0] ulps (2^23 <= n), and while n <= 2^24 it is the
-// float with exponent e and mantissa n - 2^23 (n = 2^24 gives 2^(e+1)). So
-// every bin is checked at once (thread t takes bins b + t + NT j) and the
-// walk ends at the smallest failing bin. Every thread returns the same b and
-// S. Uses misc->red_i; begins and ends at barriers of all threads.
+// The smallest v over the CTA (every thread gets it). Uses misc->red_i.
 __device__ int block_min_int(int v, Misc* m) {
     v = __reduce_min_sync(FULLMASK, v);
     if ((threadIdx.x & 31) == 0) m->red_i[threadIdx.x >> 5] = v;
@@ -578,40 +577,62 @@ __device__ int block_min_int(int v, Misc* m) {
     __syncthreads();
     return r;
 }
-__device__ int block_walk_bins(float& S, int b, int bend, const Sm& s, const int8_t* g, uint8_t plain_bit,
-                               float stop, bool record) {
-    Misc* m = s.misc;
+// Warp 0 advances S over bins [b, bend) whose k-sums (at binade g[b]) are
+// valid for the current S; stops at the first bin that needs its elements
+// (returned), or at bend. Optionally records S at each bin start. The k-sums
+// are read as the exclusive prefix E = s.ksum over the last pass's bin range
+// (prefix_ksums): within one binade of S the sum after bin b is
+// n = m + E[b+1] - E[b0] ulps (2^23 <= n), and while n <= 2^24 it is the
+// float with exponent e and mantissa n - 2^23 (n = 2^24 gives 2^(e+1)). So
+// 32 bins are checked at once (lane l takes bin base + l) and the walk ends
+// at the smallest failing bin; no block barrier. Every lane returns the same
+// b and S.
+__device__ int warp_walk_bins(float& S, int b, int bend, const Sm& s, const int8_t* g, uint8_t plain_bit, float stop,
+                              bool record) {
+    const int lane = threadIdx.x & 31;
     if (b >= bend) return bend;
-    const unsigned long long* E = s.ksum;
-    const unsigned long long lim = 1ull << 24;
-    int first = bend;
     if (!(S > 0.0f)) {
-        // before the first element S stays 0: the walk ends at the first non-empty bin
-        for (int bb = b + threadIdx.x; bb < bend; bb += NT)
-            if (s.cnt[bb] != 0) { first = bb; break; }
-        const int fb = block_min_int(first, m);
+        int fb = bend;
+        for (int base = b; base < bend; base += 32) {
+            const int bb = base + lane;
+            const uint32_t ne = __ballot_sync(FULLMASK, bb < bend && s.cnt[bb] != 0);
+            if (ne) {
+                fb = base + __ffs(ne) - 1;
+                break;
+            }
+        }
         if (record)
-            for (int bb = b + threadIdx.x; bb < fb; bb += NT) s.sstart[bb] = S;
+            for (int bb = b + lane; bb < fb; bb += 32) s.sstart[bb] = S;
         return fb;
     }
+    const unsigned long long* E = s.ksum;
+    const unsigned long long lim = 1ull << 24;
     const int e = binade(S);
     const uint32_t ebits = (uint32_t)(e + 127) << 23;
     const unsigned long long m0 = (uint32_t)__fmul_rn(S, pow2f(23 - e));
     const unsigned long long e0 = E[b];
-    for (int bb = b + threadIdx.x; bb < bend; bb += NT) {
-        const uint32_t c = s.cnt[bb];
-        const uint8_t f = s.flag[bb];
-        const bool tied = (s.tie[bb >> 5] >> (bb & 31)) & 1u;
-        const bool plain = c == 0 || ((f & plain_bit) && !(f & F_GATH) && g[bb] == e && !tied);
-        const unsigned long long pa = m0 + (E[bb] - e0), pb = m0 + (E[bb + 1] - e0);
-        const float after = __uint_as_float(ebits + (uint32_t)(pb - 0x800000ull));
-        if (!(plain && pa < lim && pb <= lim && !(after >= stop))) { first = bb; break; }
-    }
-    const int fb = block_min_int(first, m);
-    // bins b..fb were reached with the sum in this binade (n <= 2^24)
-    if (record)
-        for (int bb = b + threadIdx.x; bb <= fb && bb < bend; bb += NT)
+    int fb = bend;
+    for (int base = b; base < bend; base += 32) {
+        const int bb = base + lane;
+        bool fail = false;
+        if (bb < bend) {
+            const uint32_t c = s.cnt[bb];
+            const uint8_t f = s.flag[bb];
+            const bool tied = (s.tie[bb >> 5] >> (bb & 31)) & 1u;
+            const bool plain = c == 0 || ((f & plain_bit) && !(f & F_GATH) && g[bb] == e && !tied);
+            const unsigned long long pa = m0 + (E[bb] - e0), pb = m0 + (E[bb + 1] - e0);
+            const float after = __uint_as_float(ebits + (uint32_t)(pb - 0x800000ull));
+            fail = !(plain && pa < lim && pb <= lim && !(after >= stop));
+        }
+        const uint32_t bal = __ballot_sync(FULLMASK, fail);
+        const int last = bal ? base + __ffs(bal) - 1 : base + 31;  // bins reached in this step: up to last
+        if (record && bb < bend && bb <= last)
             s.sstart[bb] = __uint_as_float(ebits + (uint32_t)(m0 + (E[bb] - e0) - 0x800000ull));
+        if (bal) {
+            fb = last;
+            break;
+        }
+    }
     if (fb > b) S = __uint_as_float(ebits + (uint32_t)(m0 + (E[fb] - e0) - 0x800000ull));
     return fb;
 }
@@ -1874,6 +1895,20 @@ __device__ __forceinline__ void pass_elements(const RowCtx& r, const Sm& s, floa
     }
 }
 
+// Warp 0: the end of the run of gathered bins that starts at gathered bin b
+// (b < bend): the first bin from b + 1 that is empty, not gathered, a run
+// bin, or bend. The run's elements are contiguous in the sorted list.
+__device__ int gathered_run_end(const Sm& s, int b, int bend) {
+    const int lane = threadIdx.x & 31;
+    for (int base = b + 1; base < bend; base += 32) {
+        const int bb = base + lane;
+        const bool stop = bb >= bend || s.cnt[bb] == 0 || !(s.flag[bb] & F_GATH) || RUNBIN(bb);
+        const uint32_t bal = __ballot_sync(FULLMASK, stop);
+        if (bal) return base + __ffs(bal) - 1;
+    }
+    return bend;
+}
+
 __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch& a, const Sm& s) {
     Misc* m = s.misc;
     const qsamp_row_params& p = m->prm;
@@ -2089,42 +2124,48 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 go = false;
                 const int stage = w.stage;
                 if (stage == ST_SWALK) {
-                    // the bin walk by the whole CTA; a gathered bin's elements by
-                    // warp 0 and a run bin by thread 0, the sum broadcast after
-                    __shared__ float bw_S;
+                    // the walk by warp 0 alone (no block barrier per bin): plain
+                    // bins 32 at a time, a gathered bin's elements by the warp, a
+                    // run bin by lane 0 (the sum broadcast after)
                     float S = w.S;
                     int b = w.swb;
-                    while (true) {
+                    while (threadIdx.x < 32) {
                         // bins from `dead` on cannot change S (their largest term is
                         // below half an ulp of S): the walk ends there
                         const int dead = S > 0.0f ? s_dead_bin(S) : NB - 1;
-                        b = block_walk_bins(S, b, dead, s, s.gs, F_PLAINS, POS_INF, true);
+                        b = warp_walk_bins(S, b, dead, s, s.gs, F_PLAINS, POS_INF, true);
                         if (b >= dead) {
-                            for (int q = b + threadIdx.x; q < NB - 1; q += NT) s.sstart[q] = S;
+                            for (int q = b + threadIdx.x; q < NB - 1; q += 32) s.sstart[q] = S;
                             b = NB - 1;
                             break;
                         }
                         const bool runbin = RUNBIN(b);
                         if (!runbin && !(s.flag[b] & F_GATH)) break;
-                        if (threadIdx.x < 32) {
-                            if (runbin) {
-                                // one or two runs of equal terms: closed form
-                                if (threadIdx.x == 0) {
-                                    s.sstart[b] = S;
-                                    const BinRuns R = BIN_RUNS(b);
+                        if (runbin) {
+                            // one or two runs of equal terms: closed form
+                            if (threadIdx.x == 0) {
+                                s.sstart[b] = S;
+                                const BinRuns R = BIN_RUNS(b);
 #pragma unroll
-                                    for (int q = 0; q < 2; ++q)
-                                        if (q < R.n) qs_run_add(&S, R.t[q], R.c[q], POS_INF);
-                                }
-                            } else {
-                                const uint32_t off = s.specoff[b];
-                                if (threadIdx.x == 0) s.sstart[b] = S;
-                                warp_walk_terms(S, (int)s.cnt[b], POS_INF, [&](int i) { return s.spect[off + i]; });
+                                for (int q = 0; q < 2; ++q)
+                                    if (q < R.n) qs_run_add(&S, R.t[q], R.c[q], POS_INF);
                             }
-                            if (threadIdx.x == 0) bw_S = S;
+                            S = __shfl_sync(FULLMASK, S, 0);
+                        } else {
+                            // a run of gathered bins (non-empty, before `dead`): their
+                            // elements are contiguous in the sorted list, walked in one
+                            // go; each bin's start is recorded at its first element
+                            const int b2 = gathered_run_end(s, b, dead);
+                            const uint32_t off = s.specoff[b];
+                            const int nrun = (int)(s.specoff[b2 - 1] + s.cnt[b2 - 1] - off);
+                            warp_walk_terms(S, nrun, POS_INF, [&](int i) { return s.spect[off + i]; },
+                                            [&](int i, float Sb) {
+                                                const int bi = binof(__fsub_rn(comp_val(s.spec[off + i]), M));
+                                                if (i == 0 || binof(__fsub_rn(comp_val(s.spec[off + i - 1]), M)) != bi)
+                                                    s.sstart[bi] = Sb;
+                                            });
+                            b = b2 - 1;
                         }
-                        __syncthreads();
-                        S = bw_S;
                         ++b;
                     }
                     if (threadIdx.x == 0) {
@@ -2180,44 +2221,48 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     QS_SUB(r.row, 4, true);
                 } else if (stage == ST_CUMWALK) {
                     const float Sn = m->S_n;
-                    // as the S walk: bins by the whole CTA, elements by warp 0
-                    __shared__ float bw_C;
-                    __shared__ int bw_found;
+                    // as the S walk: warp 0 alone
                     float C = w.C;
                     int b = w.cwb;
                     int found = -1;
-                    while (true) {
-                        b = block_walk_bins(C, b, NB - 1, s, s.gc, F_PLAINC, p.top_p, false);
+                    while (threadIdx.x < 32) {
+                        b = warp_walk_bins(C, b, NB - 1, s, s.gc, F_PLAINC, p.top_p, false);
                         if (b >= NB - 1) break;
                         const int n = (int)s.cnt[b];
                         const bool runbin = RUNBIN(b);
                         if (!runbin && !(s.flag[b] & F_GATH)) break;
-                        if (threadIdx.x < 32) {
-                            int idx = n;
-                            if (runbin) {
-                                if (threadIdx.x == 0) {
-                                    const BinRuns R = BIN_RUNS(b);
-                                    long long before = 0;
-#pragma unroll
-                                    for (int q = 0; q < 2; ++q) {
-                                        if (q >= R.n || idx < n) continue;
-                                        const long long j = qs_run_add(&C, __fdiv_rn(R.t[q], Sn), R.c[q], p.top_p);
-                                        if (j < R.c[q]) { idx = (int)(before + j); continue; }
-                                        before += R.c[q];
-                                    }
-                                }
-                            } else {
-                                const uint32_t off = s.specoff[b];
-                                idx = warp_walk_terms(C, n, p.top_p, [&](int i) { return __fdiv_rn(s.spect[off + i], Sn); });
-                            }
+                        int idx = n;
+                        if (runbin) {
                             if (threadIdx.x == 0) {
-                                bw_C = C;
-                                bw_found = idx < n ? idx : -1;
+                                const BinRuns R = BIN_RUNS(b);
+                                long long before = 0;
+#pragma unroll
+                                for (int q = 0; q < 2; ++q) {
+                                    if (q >= R.n || idx < n) continue;
+                                    const long long j = qs_run_add(&C, __fdiv_rn(R.t[q], Sn), R.c[q], p.top_p);
+                                    if (j < R.c[q]) { idx = (int)(before + j); continue; }
+                                    before += R.c[q];
+                                }
+                            }
+                            C = __shfl_sync(FULLMASK, C, 0);
+                            idx = __shfl_sync(FULLMASK, idx, 0);
+                            found = idx < n ? idx : -1;
+                        } else {
+                            // a run of gathered bins in one walk; the cut's bin and
+                            // its index in that bin from the element it stopped at
+                            const int b2 = gathered_run_end(s, b, NB - 1);
+                            const uint32_t off = s.specoff[b];
+                            const int nrun = (int)(s.specoff[b2 - 1] + s.cnt[b2 - 1] - off);
+                            const int j =
+                                warp_walk_terms(C, nrun, p.top_p, [&](int i) { return __fdiv_rn(s.spect[off + i], Sn); });
+                            if (j < nrun) {
+                                b = binof(__fsub_rn(comp_val(s.spec[off + j]), M));
+                                found = (int)(off + (uint32_t)j - s.specoff[b]);
+                            } else {
+                                b = b2 - 1;
+                                found = -1;
                             }
                         }
-                        __syncthreads();
-                        C = bw_C;
-                        found = bw_found;
                         if (found >= 0) break;
                         ++b;
                     }
@@ -2499,6 +2544,22 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
 }
 
 // ------------------------------------------------------------ the kernel
+// The cluster kernel's next candidate row shared with the live-list kernel
+// (one thread): the front of the candidate list, then the rows that kernel
+// returned; -1 when there is none.
+__device__ int lv_claim_front(const QsLaunch& a) {
+    if (!a.lv_rows) return -1;
+    const int i = atomicAdd(&a.lv_q[0], 1);
+    if (i < a.lv_n && atomicCAS(&a.lv_taken[i], 0, 1) == 0) return a.lv_rows[i];
+    if (!a.lv_serve_returns) return -1;
+    const int nr = min(atomicAdd(&a.lv_q[2], 0), a.lv_n);
+    for (int k = 0; k < nr; ++k) {
+        const int v = atomicOr(&a.lv_ret[k], 0);  // 0: not yet written (a later launch serves it)
+        if (v > 0 && atomicCAS(&a.lv_rclaim[k], 0, 1) == 0) return v - 1;
+    }
+    return -1;
+}
+
 __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
     cg::cluster_group cl = cg::this_cluster();
     const int rank = (int)cl.block_rank();
@@ -2519,9 +2580,24 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
     // on the same stream, follow the host's rows in the list)
     const int nrows = a.rows ? a.nrows + (a.nrows_dev ? *a.nrows_dev : 0) : a.B;
     // cluster c starts with row c; later rows come from a queue (a.row_ctr,
-    // zero at launch) so that slow rows do not pile up on one cluster
-    for (int ri = cid; ri < nrows;) {
-        const int row = a.rows ? a.rows[ri] : ri;
+    // zero at launch) so that slow rows do not pile up on one cluster, and
+    // after the host's list from the candidates shared with the live-list
+    // kernel. The leading CTA's thread 0 takes the next row and pushes it
+    // into every CTA's own shared memory before a cluster barrier.
+    auto advance = [&](int ri_now, bool first) {
+        if (rank == 0 && threadIdx.x == 0) {
+            const int nri = first ? ri_now : (a.row_ctr ? ncl + atomicAdd(a.row_ctr, 1) : ri_now + ncl);
+            const int nrow = nri < nrows ? (a.rows ? a.rows[nri] : nri) : lv_claim_front(a);
+            for (int q = 0; q < CL; ++q) {
+                peer(cl, &m->next_ri, q)[0] = nri;
+                peer(cl, &m->next_row, q)[0] = nrow;
+            }
+        }
+        cl.sync();
+    };
+    cl.sync();  // (every CTA of the cluster has started before the first remote store)
+    advance(cid, true);
+    for (int ri = m->next_ri, row = m->next_row; row >= 0;) {
         if (threadIdx.x == 0) m->prm = a.params[row];
         __syncthreads();
         const qsamp_row_params& p = m->prm;
@@ -2632,12 +2708,9 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
             const bool stop = m->skip_row >= 2;
             cl.sync();
             if (stop) return;
-            if (a.row_ctr && rank == 0 && threadIdx.x == 0) {
-                const int nx = ncl + atomicAdd(a.row_ctr, 1);
-                for (int q = 0; q < CL; ++q) peer(cl, &m->next_ri, q)[0] = nx;
-            }
-            cl.sync();
-            ri = a.row_ctr ? m->next_ri : ri + ncl;
+            advance(ri, false);
+            ri = m->next_ri;
+            row = m->next_row;
             continue;
         }
 
@@ -2689,14 +2762,11 @@ __global__ void __launch_bounds__(NT, 1) qs_rows_kernel(QsLaunch a) {
         }
         __syncthreads();
         QS_TMARK(row, 4, rank == 0);
-        if (a.row_ctr && rank == 0 && threadIdx.x == 0) {
-            // pushed into every CTA's own shared memory before the barrier:
-            // no CTA reads a peer after the cluster's last barrier
-            const int nx = ncl + atomicAdd(a.row_ctr, 1);
-            for (int q = 0; q < CL; ++q) peer(cl, &m->next_ri, q)[0] = nx;
-        }
-        cl.sync();
-        ri = a.row_ctr ? m->next_ri : ri + ncl;
+        // (pushed into every CTA's own shared memory before the barrier: no
+        // CTA reads a peer after the cluster's last barrier)
+        advance(ri, false);
+        ri = m->next_ri;
+        row = m->next_row;
     }
 }
 
@@ -3579,6 +3649,7 @@ __global__ void qs_verify_kernel(const void* logits, int dtype, long long row_st
 }
 
 #include "qsamp_hist.cuh"
+#include "qsamp_live.cuh"
 
 }  // namespace qs
 
@@ -3686,6 +3757,15 @@ extern "C" cudaError_t qs_hist_attrs(size_t smem) {
 }
 extern "C" cudaError_t qs_launch_hist(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st) {
     qs::qs_hist_kernel<<<grid, qs::HS_NT, smem, st>>>(*a);
+    return cudaGetLastError();
+}
+extern "C" size_t qs_live_smem() { return (size_t)qs::lv_layout().total; }
+extern "C" int qs_live_vmax() { return qs::LV_VMAX; }
+extern "C" cudaError_t qs_live_attrs(size_t smem) {
+    return cudaFuncSetAttribute(qs::qs_live_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+extern "C" cudaError_t qs_launch_live(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st) {
+    qs::qs_live_kernel<<<grid, qs::HS_NT, smem, st>>>(*a);
     return cudaGetLastError();
 }
 extern "C" cudaError_t qs_launch_stream(const qs::QsLaunch* a, int grid, size_t smem, cudaStream_t st) {

@@ -121,6 +121,11 @@ class _Counters(ctypes.Structure):
         ("last_hist_rows", ctypes.c_int32),
         ("last_hist_handed_on", ctypes.c_int32),
         ("last_hist_kernel_ms", ctypes.c_double),
+        ("last_live_candidates", ctypes.c_int32),
+        ("last_live_rows", ctypes.c_int32),
+        ("last_live_returned", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("last_live_kernel_ms", ctypes.c_double),
     ]
 
 
@@ -130,7 +135,7 @@ class _Limits(ctypes.Structure):
         ("drop_ready_from", ctypes.c_int32),
         ("ready_wait_ns", ctypes.c_int64),
         ("hist_path", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("live_path", ctypes.c_int32),
     ]
 
 
@@ -351,7 +356,8 @@ class Context:
         self._check(self.lib.qsamp_get_limits(self.h, ctypes.byref(lim)), "qsamp_get_limits")
         return {f: getattr(lim, f) for f, _ in lim._fields_}
 
-    def set_limits(self, max_rounds=None, ready_wait_ns=None, drop_ready_from=None, hist_path=None) -> None:
+    def set_limits(self, max_rounds=None, ready_wait_ns=None, drop_ready_from=None, hist_path=None,
+                   live_path=None) -> None:
         """qsamp_set_limits; arguments left None keep their current value."""
         cur = self.limits()
         lim = _Limits()
@@ -359,6 +365,7 @@ class Context:
         lim.ready_wait_ns = cur["ready_wait_ns"] if ready_wait_ns is None else int(ready_wait_ns)
         lim.drop_ready_from = cur["drop_ready_from"] if drop_ready_from is None else int(drop_ready_from)
         lim.hist_path = cur["hist_path"] if hist_path is None else int(hist_path)
+        lim.live_path = cur["live_path"] if live_path is None else int(live_path)
         self._check(self.lib.qsamp_set_limits(self.h, ctypes.byref(lim)), "qsamp_set_limits")
 
     def verify_greedy(self, logits, row_off, drafts, eos_token: int = -1, stream=None):
