@@ -530,16 +530,8 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
     int32_t* wid = (int32_t*)(smem_raw + L.off_wid);
     uint64_t* exp32 = (uint64_t*)(smem_raw + L.off_exp);
     Misc* m = (Misc*)(smem_raw + L.off_misc);
-    float* sA = (float*)(H + HO_SA);
-    unsigned long long* inc = (unsigned long long*)(H + HO_INC);
-    float* sB = (float*)(H + HO_SB);
-    int* stp = (int*)(H + HO_STP);
     unsigned long long* pref = (unsigned long long*)(H + HO_PREF);
     unsigned long long* wk = (unsigned long long*)(H + HO_WK);
-    u128* inc2 = (u128*)(H + HO_INC2);
-    double* wd = (double*)(H + HO_WD);
-    double* sC = (double*)(H + HO_SC);
-    uint32_t* gcd = (uint32_t*)(H + HO_GCD);
     int* wm = (int*)(H + HO_WM);
     __shared__ HsMisc hm;
     __shared__ unsigned long long wtot[NWARPS];
@@ -868,7 +860,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             }
             const float S1 = dr.S1, S2 = dr.S2, prob = dr.prob;
             const long long n_keep = dr.n_keep, pos = dr.pos;
-            const int gp = dr.gp, jc = dr.jc, it_s = dr.it_s, it_c = dr.it_c, it_d = dr.it_d;
+            const int gp = dr.gp;
             // ---- 7. the element at sorted position pos: the first group of
             // its value, its rank among the row's elements of that value
             // (ascending id), and the element of that rank
@@ -1007,10 +999,10 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             __syncthreads();
             QS_TMARK(row, 8, true);
             QS_NOTE(row, 9, G, true);
-            QS_NOTE(row, 11, it_s, true);
-            QS_NOTE(row, 12, it_c, true);
-            QS_NOTE(row, 13, it_d, true);
-            QS_NOTE(row, 14, jc + 1, true);
+            QS_NOTE(row, 11, dr.it_s, true);
+            QS_NOTE(row, 12, dr.it_c, true);
+            QS_NOTE(row, 13, dr.it_d, true);
+            QS_NOTE(row, 14, dr.jc + 1, true);
             if (hm.found_id < 0) {  // (not expected: the groups count these elements)
                 hs_bail(a, row);
                 goto next_row;
