@@ -69,7 +69,8 @@ __host__ __device__ inline HsLayout hs_layout() {
 // The walks' arrays inside the histogram's 128 KB (byte offsets), free once
 // the groups are built:
 //   walks A/B: sA float[GMAX] 0 | inc u64[GMAX] 16K | sB float[GMAX] 48K | stp int[GMAX] 64K
-//   all along: pref u64[GMAX] 80K (group start positions) | wk u64[WMAX] 112K (window sort)
+//   all along: pref u64[GMAX] 80K (group start positions) | wk u64[WMAX] 112K (window keys)
+//   until the sums: the window keys in descending order, u64[WMAX] 16K
 //   the draw (after sum_keep): inc2 u128[DMAX] 0 | wd double[DMAX] 32K | sC double[DMAX] 48K
 //              | stp (first DMAX) 64K | gcd u32[DMAX] 120K
 //   the recovery: wm int[WMAX] 0
@@ -97,8 +98,30 @@ __device__ __forceinline__ uint32_t hs_count(const uint32_t* hist, int k) {
 
 struct HsMisc {
     float M, S1, S2;
-    int nuniq, bail, changed, top_key, found_id, nwm, next_ri, kmin;
+    int nuniq, bail, changed, top_key, found_id, nwm, next_ri, kmin, klo, khi;
 };
+
+// The smallest k in [lo, hi) with pred(k), or hi, for a pred that is false
+// and then true over the range: a 32-way search by one warp (every lane gets
+// the answer). The smallest such k stays in [lo, hi] (hi: none); each round
+// tests 31 points evenly spread over the range, the last standing for hi.
+template <typename P>
+__device__ int hs_warp_search(int lo, int hi, P pred) {
+    const int lane = threadIdx.x & 31;
+    while (hi - lo > 32) {
+        const int pt = lo + (int)(((long long)(hi - lo) * (lane + 1)) / 32);  // lane 31: hi
+        const bool t = pt < hi && pred(pt);
+        const uint32_t bt = __ballot_sync(FULLMASK, t) | 0x80000000u;
+        const int f = __ffs(bt) - 1;  // first point at which pred holds (31: hi)
+        const int pf = lo + (int)(((long long)(hi - lo) * (f + 1)) / 32);
+        const int pp = f > 0 ? lo + (int)(((long long)(hi - lo) * f) / 32) + 1 : lo;
+        lo = pp;
+        hi = pf;
+    }
+    const int kk = lo + lane;
+    const uint32_t bt = __ballot_sync(FULLMASK, kk < hi && pred(kk));
+    return bt ? lo + __ffs(bt) - 1 : hi;
+}
 
 // Exclusive scan, in place, of n <= HS_GMAX u64 values; returns the total.
 // Thread t owns entries [t*HS_GPT, (t+1)*HS_GPT).
@@ -393,15 +416,39 @@ __device__ bool hs_sums_draw(const QsLaunch& a, int row, const qsamp_row_params&
     hs_scan_u64(inc, G, wtot);
     for (int g = threadIdx.x; g < G; g += HS_NT) sA[g] = g == 0 ? 0.0f : units_f(inc[g], 30);
     __syncthreads();
+    QS_TMARK(row, 19, true);
     o.it_s = o.it_c = o.it_d = 0;
-    if (!hs_walk_f(G, gc, gt, sA, inc, nullptr, POS_INF, 23, wtot, &hm, &o.it_s)) return false;
-    if (threadIdx.x == 0) {
-        float S = sA[G - 1];
-        qs_run_add(&S, gt[G - 1], (long long)gc[G - 1], POS_INF);
-        hm.S1 = S;
+    // Groups whose term is below half an ulp of the running sum add nothing,
+    // and neither does any later one (smaller terms, a larger sum): the walk
+    // covers the groups before the first whose term is below a quarter ulp
+    // of its guessed start (the float sum stays within a factor 2 of the
+    // real-valued one), checks the bound at the exact sum it reaches, and
+    // walks every group if the check fails.
+    int nlive = G;
+    for (int g = threadIdx.x; g < G; g += HS_NT) {
+        const uint32_t sb = __float_as_uint(sA[g]);
+        if (g > 0 && sb >= (26u << 23) && gt[g] < __uint_as_float((sb & 0x7f800000u) - (25u << 23))) nlive = min(nlive, g);
     }
-    __syncthreads();
+    nlive = block_min_int(nlive, m);
+    while (true) {
+        if (!hs_walk_f(nlive, gc, gt, sA, inc, nullptr, POS_INF, 23, wtot, &hm, &o.it_s)) return false;
+        if (threadIdx.x == 0) {
+            float S = sA[nlive - 1];
+            qs_run_add(&S, gt[nlive - 1], (long long)gc[nlive - 1], POS_INF);
+            hm.S1 = S;
+            // the first group left out must be below half an ulp of the sum
+            const uint32_t sb = __float_as_uint(S);
+            hm.changed = nlive < G && !(gt[nlive] < __uint_as_float((sb & 0x7f800000u) - (24u << 23)));
+        }
+        __syncthreads();
+        if (!hm.changed || nlive == G) break;
+        nlive = G;  // (the starts walked so far are exact; the rest keep their guesses)
+        __syncthreads();
+    }
     const float S1 = hm.S1;
+    // the starts of the groups left out: the final sum (sum_keep reads them)
+    for (int g = nlive + threadIdx.x; g < G; g += HS_NT) sA[g] = S1;
+    __syncthreads();
     QS_TMARK(row, 5, true);
 
     // ---- the top-p cut: cum += t / sum_exp until cum >= top_p (:173-178)
@@ -532,6 +579,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
     Misc* m = (Misc*)(smem_raw + L.off_misc);
     unsigned long long* pref = (unsigned long long*)(H + HO_PREF);
     unsigned long long* wk = (unsigned long long*)(H + HO_WK);
+    unsigned long long* wks = (unsigned long long*)(H + HO_INC);  // the window's keys sorted (until the sums)
     int* wm = (int*)(H + HO_WM);
     __shared__ HsMisc hm;
     __shared__ unsigned long long wtot[NWARPS];
@@ -746,6 +794,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 if (lane == 0) hm.kmin = bt ? lo + __ffs(bt) - 1 : hi;
             }
             __syncthreads();
+            QS_TMARK(row, 15, true);
             const int kmin = hm.kmin;
             const int ktop = hm.top_key;
             const int nkeys = ktop >= kmin ? ktop - kmin + 1 : 0;
@@ -762,16 +811,20 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 goto next_row;
             }
             {
+                // the keys first (the non-empty ones crowd into a few threads'
+                // ranges), their values after, spread over every thread
                 int at = off;
                 for (int k = khi_t; k > klo_t; --k) {
                     const uint32_t c = hs_count(hist, k);
                     if (!c) continue;
-                    gx[at] = hs_value(r, (uint32_t)k);
+                    gx[at] = __int_as_float(k);
                     gc[at] = c;
                     ++at;
                 }
             }
             __syncthreads();  // (the histogram is read no more)
+            for (int g = threadIdx.x; g < npg; g += HS_NT) gx[g] = hs_value(r, (uint32_t)__float_as_int(gx[g]));
+            QS_TMARK(row, 16, true);
             int nw = 0;
             {
                 int mw = 0;
@@ -781,11 +834,16 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                 for (int u = threadIdx.x; u < nuniq; u += HS_NT)
                     if (wx[u] > NEG_INF && __fsub_rn(wx[u], M) >= HS_DMIN)
                         wk[o2++] = ((unsigned long long)qs_key(wx[u]) << 32) | (uint32_t)u;
-                const int P2 = next_pow2(nw > 1 ? nw : 1);
                 __syncthreads();
-                for (int i = nw + threadIdx.x; i < P2; i += HS_NT) wk[i] = 0ull;
-                __syncthreads();
-                if (P2 > 1) bitonic_desc<128>(wk, P2);
+                // descending order by counting (the keys are distinct: the low
+                // word is the entry's index); every thread reads the same key
+                // at a time (a shared-memory broadcast)
+                for (int j = threadIdx.x; j < nw; j += HS_NT) {
+                    const unsigned long long kj = wk[j];
+                    int rk = 0;
+                    for (int i = 0; i < nw; ++i) rk += wk[i] > kj;
+                    wks[rk] = kj;
+                }
                 __syncthreads();
             }
             const int G = npg + nw;
@@ -808,7 +866,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                         int lo = 0, hi = nw;  // first window entry with value <= px
                         while (lo < hi) {
                             const int mid = (lo + hi) >> 1;
-                            if (qs_unkey((uint32_t)(wk[mid] >> 32)) > px[e]) lo = mid + 1;
+                            if (qs_unkey((uint32_t)(wks[mid] >> 32)) > px[e]) lo = mid + 1;
                             else hi = mid;
                         }
                         pd[e] = i + lo;
@@ -822,7 +880,7 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                     wdst[e] = -1;
                     wv[e] = 0.0f;
                     if (j < nw) {
-                        wv[e] = qs_unkey((uint32_t)(wk[j] >> 32));
+                        wv[e] = qs_unkey((uint32_t)(wks[j] >> 32));
                         int lo = 0, hi = npg;  // first pattern group with value < wv
                         while (lo < hi) {
                             const int mid = (lo + hi) >> 1;
@@ -847,11 +905,13 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                     }
                 __syncthreads();
             }
+            QS_TMARK(row, 17, true);
             // group start positions in the sorted row
             for (int g = threadIdx.x; g < G; g += HS_NT) pref[g] = gc[g];
             __syncthreads();
             hs_scan_u64(pref, G, wtot);
 
+            QS_TMARK(row, 18, true);
             // ---- 6. the sums and the draw over the groups
             HsDrawn dr;
             if (!hs_sums_draw(a, row, p, G, gx, gc, gt, hs_arrays(H), exp32, M, hm, wtot, wtot2, m, dr)) {
@@ -868,24 +928,22 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             int glo = gp;
             while (glo > 0 && gx[glo - 1] == xs) --glo;
             const long long rank = pos - (long long)pref[glo];
+            // the row's elements of value xs (the groups of that value): the
+            // search below counts from the nearer end of the row
+            int ghi = gp;
+            while (ghi + 1 < G && gx[ghi + 1] == xs) ++ghi;
+            const long long n_xs = (ghi + 1 < G ? (long long)pref[ghi + 1] : (long long)pref[ghi] + gc[ghi]) -
+                                   (long long)pref[glo];
+            const bool from_end = 2 * rank >= n_xs;
+            const long long target = from_end ? n_xs - 1 - rank : rank;
             // the keys whose (non-window) elements have value xs: [klo, khi]
-            int klo, khi;
-            {
-                int lo = HS_KLO, hi = HS_KHI;  // first key with value >= xs
-                while (lo < hi) {
-                    const int mid = (lo + hi) >> 1;
-                    if (hs_value(r, (uint32_t)mid) < xs) lo = mid + 1;
-                    else hi = mid;
-                }
-                klo = lo;
-                hi = HS_KHI;  // first key with value > xs
-                while (lo < hi) {
-                    const int mid = (lo + hi) >> 1;
-                    if (hs_value(r, (uint32_t)mid) <= xs) lo = mid + 1;
-                    else hi = mid;
-                }
-                khi = lo - 1;
-            }
+            // (the key -> value map is monotone: two 32-way searches, one warp each)
+            if (threadIdx.x < 32)
+                hm.klo = hs_warp_search(HS_KLO, HS_KHI, [&](int k) { return hs_value(r, (uint32_t)k) >= xs; });
+            else if (threadIdx.x < 64)
+                hm.khi = hs_warp_search(HS_KLO, HS_KHI, [&](int k) { return hs_value(r, (uint32_t)k) > xs; }) - 1;
+            __syncthreads();
+            const int klo = hm.klo, khi = hm.khi;
             // the window's elements of value xs (allowed ones: -inf never equals xs)
             for (int u = threadIdx.x; u < nuniq; u += HS_NT)
                 if (wx[u] == xs) wm[atomicAdd(&hm.nwm, 1)] = wid[u];
@@ -936,11 +994,16 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             // elements: warp w counts elements [s + 1024 w, s + 1024 (w + 1))
             // in four 256-element pieces (their loads in flight together); one
             // prefix over the warps tells whether the rank-th lies in this
-            // super-chunk, and which warp and piece hold it
+            // super-chunk, and which warp and piece hold it. Super-chunks are
+            // taken from the end of the row down when the rank-th is nearer
+            // the end (target counts from there; inside the super-chunk that
+            // holds it the rank is counted forward again).
             {
                 const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+                const int nsc = (V + NWARPS * 1024 - 1) / (NWARPS * 1024);
                 long long acc = 0;
-                for (int sc = 0; sc < V; sc += NWARPS * 1024) {
+                for (int q = 0; q < nsc; ++q) {
+                    const int sc = (from_end ? nsc - 1 - q : q) * (NWARPS * 1024);
                     const int wb = sc + warp * 1024;
                     uint4 qv[4];
 #pragma unroll
@@ -956,17 +1019,18 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
                     }
                     if (lane == 0) hs_wc[warp] = pc[0] + pc[1] + pc[2] + pc[3];
                     __syncthreads();
-                    long long before = acc;
-                    int tot = 0;
-                    for (int q = 0; q < NWARPS; ++q) {
-                        if (q < warp) before += hs_wc[q];
-                        tot += hs_wc[q];
+                    int before = 0, tot = 0;  // (within the super-chunk)
+                    for (int w2 = 0; w2 < NWARPS; ++w2) {
+                        if (w2 < warp) before += hs_wc[w2];
+                        tot += hs_wc[w2];
                     }
                     __syncthreads();  // (hs_wc is rewritten by the next super-chunk)
-                    if (acc + tot > rank) {
+                    if (acc + tot > target) {
+                        // the forward rank inside this super-chunk
+                        const int lr = from_end ? (int)(tot - 1 - (target - acc)) : (int)(target - acc);
                         const int wc = pc[0] + pc[1] + pc[2] + pc[3];
-                        if (rank >= before && rank < before + wc) {
-                            int want = (int)(rank - before);
+                        if (lr >= before && lr < before + wc) {
+                            int want = lr - before;
                             int u = 0;
                             while (u < 3 && want >= pc[u]) want -= pc[u++];
                             uint32_t f = fl[0];
