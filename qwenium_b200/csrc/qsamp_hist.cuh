@@ -44,6 +44,7 @@ constexpr int HS_WMAX = 1024;        // penalty window served
 constexpr int HS_HT = 2048;          // window hash slots
 constexpr int HS_ITERS = 24;         // scan passes before a row is handed on
 constexpr float HS_DMIN = -17.5f;    // x - M below this: expf < 2^-25, no sum sees it
+constexpr int HS_LD = 8;             // 16-byte loads in flight per thread in the histogram pass
 constexpr int HS_KLO = 128, HS_KHI = 65408;  // keys of finite bf16 values: [HS_KLO, HS_KHI)
 static_assert(HS_GMAX % HS_NT == 0 && HS_DMAX % HS_NT == 0, "groups per thread");
 
@@ -645,15 +646,15 @@ __global__ void __launch_bounds__(HS_NT, 1) qs_hist_kernel(QsLaunch a) {
             // ---- 2. the row, once: allow-mask and histogram by key
             int ninf = 0;
             const int nvec = a.vec_ok ? V / 8 : 0;
-            for (int g0 = threadIdx.x; g0 < nvec; g0 += 4 * HS_NT) {
-                uint4 q[4];
+            for (int g0 = threadIdx.x; g0 < nvec; g0 += HS_LD * HS_NT) {
+                uint4 q[HS_LD];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < HS_LD; ++u) {
                     const int g = g0 + u * HS_NT;
                     q[u] = g < nvec ? __ldg((const uint4*)(rp + 8 * g)) : make_uint4(0u, 0u, 0u, 0u);
                 }
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < HS_LD; ++u) {
                     const int g = g0 + u * HS_NT;
                     if (g < nvec) {
                         const int i0 = 8 * g;
