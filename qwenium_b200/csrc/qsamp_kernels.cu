@@ -577,65 +577,54 @@ __device__ int block_min_int(int v, Misc* m) {
     __syncthreads();
     return r;
 }
-// Warp 0 advances S over bins [b, bend) whose k-sums (at binade g[b]) are
-// valid for the current S; stops at the first bin that needs its elements
-// (returned), or at bend. Optionally records S at each bin start. The k-sums
-// are read as the exclusive prefix E = s.ksum over the last pass's bin range
-// (prefix_ksums): within one binade of S the sum after bin b is
+// The whole CTA advances S over bins [b, bend) whose k-sums (at binade g[b])
+// are valid for the current S; stops at the first bin that needs its
+// elements (returned), or at bend. Optionally records S at each bin start.
+// The k-sums are read as the exclusive prefix E = s.ksum over the last pass's
+// bin range (prefix_ksums): within one binade of S the sum after bin b is
 // n = m + E[b+1] - E[b0] ulps (2^23 <= n), and while n <= 2^24 it is the
 // float with exponent e and mantissa n - 2^23 (n = 2^24 gives 2^(e+1)). So
-// 32 bins are checked at once (lane l takes bin base + l) and the walk ends
-// at the smallest failing bin; no block barrier. Every lane returns the same
-// b and S.
-__device__ int warp_walk_bins(float& S, int b, int bend, const Sm& s, const int8_t* g, uint8_t plain_bit, float stop,
-                              bool record) {
-    const int lane = threadIdx.x & 31;
+// every bin is checked at once (thread t takes bins b + t + NT j) and the
+// walk ends at the smallest failing bin. Every thread returns the same b and
+// S. Uses misc->red_i; begins and ends at barriers of all threads.
+__device__ int block_walk_bins(float& S, int b, int bend, const Sm& s, const int8_t* g, uint8_t plain_bit,
+                               float stop, bool record) {
+    Misc* m = s.misc;
     if (b >= bend) return bend;
-    if (!(S > 0.0f)) {
-        int fb = bend;
-        for (int base = b; base < bend; base += 32) {
-            const int bb = base + lane;
-            const uint32_t ne = __ballot_sync(FULLMASK, bb < bend && s.cnt[bb] != 0);
-            if (ne) {
-                fb = base + __ffs(ne) - 1;
-                break;
-            }
-        }
-        if (record)
-            for (int bb = b + lane; bb < fb; bb += 32) s.sstart[bb] = S;
-        return fb;
-    }
     const unsigned long long* E = s.ksum;
     const unsigned long long lim = 1ull << 24;
+    int first = bend;
+    if (!(S > 0.0f)) {
+        // before the first element S stays 0: the walk ends at the first non-empty bin
+        for (int bb = b + threadIdx.x; bb < bend; bb += NT)
+            if (s.cnt[bb] != 0) { first = bb; break; }
+        const int fb = block_min_int(first, m);
+        if (record)
+            for (int bb = b + threadIdx.x; bb < fb; bb += NT) s.sstart[bb] = S;
+        return fb;
+    }
     const int e = binade(S);
     const uint32_t ebits = (uint32_t)(e + 127) << 23;
     const unsigned long long m0 = (uint32_t)__fmul_rn(S, pow2f(23 - e));
     const unsigned long long e0 = E[b];
-    int fb = bend;
-    for (int base = b; base < bend; base += 32) {
-        const int bb = base + lane;
-        bool fail = false;
-        if (bb < bend) {
-            const uint32_t c = s.cnt[bb];
-            const uint8_t f = s.flag[bb];
-            const bool tied = (s.tie[bb >> 5] >> (bb & 31)) & 1u;
-            const bool plain = c == 0 || ((f & plain_bit) && !(f & F_GATH) && g[bb] == e && !tied);
-            const unsigned long long pa = m0 + (E[bb] - e0), pb = m0 + (E[bb + 1] - e0);
-            const float after = __uint_as_float(ebits + (uint32_t)(pb - 0x800000ull));
-            fail = !(plain && pa < lim && pb <= lim && !(after >= stop));
-        }
-        const uint32_t bal = __ballot_sync(FULLMASK, fail);
-        const int last = bal ? base + __ffs(bal) - 1 : base + 31;  // bins reached in this step: up to last
-        if (record && bb < bend && bb <= last)
-            s.sstart[bb] = __uint_as_float(ebits + (uint32_t)(m0 + (E[bb] - e0) - 0x800000ull));
-        if (bal) {
-            fb = last;
-            break;
-        }
+    for (int bb = b + threadIdx.x; bb < bend; bb += NT) {
+        const uint32_t c = s.cnt[bb];
+        const uint8_t f = s.flag[bb];
+        const bool tied = (s.tie[bb >> 5] >> (bb & 31)) & 1u;
+        const bool plain = c == 0 || ((f & plain_bit) && !(f & F_GATH) && g[bb] == e && !tied);
+        const unsigned long long pa = m0 + (E[bb] - e0), pb = m0 + (E[bb + 1] - e0);
+        const float after = __uint_as_float(ebits + (uint32_t)(pb - 0x800000ull));
+        if (!(plain && pa < lim && pb <= lim && !(after >= stop))) { first = bb; break; }
     }
+    const int fb = block_min_int(first, m);
+    // bins b..fb were reached with the sum in this binade (n <= 2^24)
+    if (record)
+        for (int bb = b + threadIdx.x; bb <= fb && bb < bend; bb += NT)
+            s.sstart[bb] = __uint_as_float(ebits + (uint32_t)(m0 + (E[bb] - e0) - 0x800000ull));
     if (fb > b) S = __uint_as_float(ebits + (uint32_t)(m0 + (E[fb] - e0) - 0x800000ull));
     return fb;
 }
+
 
 // ------------------------------------------------------------ row transform
 struct RowCtx {
@@ -2124,24 +2113,27 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                 go = false;
                 const int stage = w.stage;
                 if (stage == ST_SWALK) {
-                    // the walk by warp 0 alone (no block barrier per bin): plain
-                    // bins 32 at a time, a gathered bin's elements by the warp, a
-                    // run bin by lane 0 (the sum broadcast after)
+                    // plain bins by the whole CTA at once; a run bin by lane 0
+                    // of warp 0, a run of gathered bins by warp 0 (one barrier
+                    // per run, the sum broadcast after)
+                    __shared__ float hw_S;
+                    __shared__ int hw_b;
                     float S = w.S;
                     int b = w.swb;
-                    while (threadIdx.x < 32) {
+                    while (true) {
                         // bins from `dead` on cannot change S (their largest term is
                         // below half an ulp of S): the walk ends there
                         const int dead = S > 0.0f ? s_dead_bin(S) : NB - 1;
-                        b = warp_walk_bins(S, b, dead, s, s.gs, F_PLAINS, POS_INF, true);
+                        b = block_walk_bins(S, b, dead, s, s.gs, F_PLAINS, POS_INF, true);
                         if (b >= dead) {
-                            for (int q = b + threadIdx.x; q < NB - 1; q += 32) s.sstart[q] = S;
+                            for (int q = b + threadIdx.x; q < NB - 1; q += NT) s.sstart[q] = S;
                             b = NB - 1;
                             break;
                         }
                         const bool runbin = RUNBIN(b);
                         if (!runbin && !(s.flag[b] & F_GATH)) break;
-                        if (runbin) {
+                        if (threadIdx.x >= 32) {
+                        } else if (runbin) {
                             // one or two runs of equal terms: closed form
                             if (threadIdx.x == 0) {
                                 s.sstart[b] = S;
@@ -2166,7 +2158,13 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                                             });
                             b = b2 - 1;
                         }
-                        ++b;
+                        if (threadIdx.x == 0) {
+                            hw_S = S;
+                            hw_b = b;
+                        }
+                        __syncthreads();
+                        S = hw_S;
+                        b = hw_b + 1;
                     }
                     if (threadIdx.x == 0) {
                         w.S = S;
@@ -2221,18 +2219,22 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                     QS_SUB(r.row, 4, true);
                 } else if (stage == ST_CUMWALK) {
                     const float Sn = m->S_n;
-                    // as the S walk: warp 0 alone
+                    // as the S walk: plain bins by the CTA, a run bin or a run of
+                    // gathered bins by warp 0
+                    __shared__ float hw_C;
+                    __shared__ int hw_cb, hw_found;
                     float C = w.C;
                     int b = w.cwb;
                     int found = -1;
-                    while (threadIdx.x < 32) {
-                        b = warp_walk_bins(C, b, NB - 1, s, s.gc, F_PLAINC, p.top_p, false);
+                    while (true) {
+                        b = block_walk_bins(C, b, NB - 1, s, s.gc, F_PLAINC, p.top_p, false);
                         if (b >= NB - 1) break;
                         const int n = (int)s.cnt[b];
                         const bool runbin = RUNBIN(b);
                         if (!runbin && !(s.flag[b] & F_GATH)) break;
                         int idx = n;
-                        if (runbin) {
+                        if (threadIdx.x >= 32) {
+                        } else if (runbin) {
                             if (threadIdx.x == 0) {
                                 const BinRuns R = BIN_RUNS(b);
                                 long long before = 0;
@@ -2263,6 +2265,15 @@ __device__ void full_path(cg::cluster_group& cl, const RowCtx& r, const QsLaunch
                                 found = -1;
                             }
                         }
+                        if (threadIdx.x == 0) {
+                            hw_C = C;
+                            hw_cb = b;
+                            hw_found = found;
+                        }
+                        __syncthreads();
+                        C = hw_C;
+                        b = hw_cb;
+                        found = hw_found;
                         if (found >= 0) break;
                         ++b;
                     }
