@@ -125,6 +125,15 @@ struct qsamp_ctx {
     int use_live = 0;
     bool live_attr = false;
     size_t attrs_smem = 0;
+    // clusters the device can place, per cluster size of plan_for, for each
+    // (V, layout) seen: device queries that would otherwise run on every call
+    struct ClusterOcc {
+        int V;
+        bool vcounts;
+        size_t max_dyn;
+        int mc[10];
+    };
+    std::vector<ClusterOcc> occ;
     size_t max_dyn = 0;    // largest dynamic shared memory a CTA of the kernel may use
     qsamp_counters ctr = {};
     // optional per-kernel device timing: begin / end events of the stream,
@@ -200,19 +209,35 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, bool vcounts, Plan& out) {
     if (first < 0)
         return fail(c, QSAMP_ERR_UNSUPPORTED, "V=%d exceeds the largest vocabulary one 16-CTA cluster holds (%d)", V,
                     16 * (int)((c->max_dyn - (size_t)qs::smem_layout(0, vcounts).total) / 4 / 8 * 8));
+    // the clusters of each size the device can place (queried once per
+    // (V, layout) and context)
+    const int* mcs = nullptr;
+    for (const auto& o : c->occ)
+        if (o.V == V && o.vcounts == vcounts && o.max_dyn == c->max_dyn) mcs = o.mc;
+    if (!mcs) {
+        qsamp_ctx::ClusterOcc o;
+        o.V = V;
+        o.vcounts = vcounts;
+        o.max_dyn = c->max_dyn;
+        for (int i = 0; i < 10; ++i) {
+            o.mc[i] = 0;
+            if (i < first) continue;
+            const int cl = sizes[i];
+            const int n_s = qs::align_up((V + cl - 1) / cl, 8);
+            const size_t smem = (size_t)qs::smem_layout(n_s, vcounts).total;
+            if (qs_max_clusters(cl, smem, &o.mc[i]) != cudaSuccess) {
+                cudaGetLastError();
+                o.mc[i] = 0;
+            }
+        }
+        c->occ.push_back(o);
+        mcs = c->occ.back().mc;
+    }
     // (a size the device reports it cannot place -- no cluster of it fits,
     // whatever the reason -- gives way to the next, smaller slices)
     int pick = -1;
     for (int i = first; i < 10; ++i) {
-        const int cl = sizes[i];
-        const int n_s = qs::align_up((V + cl - 1) / cl, 8);
-        const size_t smem = (size_t)qs::smem_layout(n_s, vcounts).total;
-        int mc = 0;
-        cudaError_t e = qs_max_clusters(cl, smem, &mc);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            mc = 0;
-        }
+        const int mc = mcs[i];
         if (mc <= 0) {
             if (pick < 0) continue;
             break;
@@ -226,10 +251,7 @@ qsamp_status plan_for(qsamp_ctx* c, int B, int V, bool vcounts, Plan& out) {
     out.cl = cl;
     out.n_s = qs::align_up((V + cl - 1) / cl, 8);
     out.smem = (size_t)qs::smem_layout(out.n_s, vcounts).total;
-    int mc = 0;
-    cudaError_t e = qs_max_clusters(cl, out.smem, &mc);
-    if (e != cudaSuccess || mc <= 0)
-        return cuda_fail(c, e == cudaSuccess ? cudaErrorInvalidConfiguration : e, "cudaOccupancyMaxActiveClusters");
+    const int mc = mcs[pick];
     out.clusters = mc < B ? mc : B;
     return QSAMP_OK;
 }
